@@ -1,0 +1,140 @@
+// mdq_math.cuh - per-element arithmetic of the MDQ-AdamW step.
+//
+// Every expression here reproduces, operation for operation, the arithmetic of
+// the reference kernel family (ruby320/STREAM-MM2026 CUDA/stquant_kernel.cu:
+// 53-401) as its -O3 build evaluates it: nvcc contracts a*b+c into one fused
+// multiply-add, so each contraction is written out with __fmaf_rn (which the
+// compiler never re-associates) and every other operation with its correctly
+// rounded intrinsic.  CUDA's own expf / logf / powf / sqrtf / pow are called,
+// never re-derived, so the transcendental results are those of the reference.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mdq {
+
+// Per-tensor constants, computed once per CTA when it starts a tensor.
+struct StepConsts {
+    float b1, omb1, b2, omb2;  // beta1, 1-beta1, beta2, 1-beta2
+    float eps;
+    float wd;                  // weight decay (0 disables the decay multiply)
+    float decay;               // 1 - lr*wd                (contracted)
+    float step_size;           // lr / bc1                 (IEEE divide)
+    float sqrt_bc2;            // sqrtf(1 - beta2^step)    (IEEE sqrt)
+    float inv_sqrt_bc2;        // 1 / sqrt_bc2             (fast p mode only)
+    float lm_f, lv_f;          // (float)2^(m_bits-1), (float)(2^v_bits - 1)
+    double lm_d, lv_d;         // the same levels in double, for clamping
+};
+
+// CUDA/stquant_kernel.cu:88-89 (levels), :136-141 (bias correction, decay).
+__device__ __forceinline__ StepConsts make_step_consts(float b1, float b2, float lr, float wd,
+                                                       float eps, int step, int m_bits,
+                                                       int v_bits) {
+    StepConsts c;
+    c.b1 = b1;
+    c.b2 = b2;
+    c.omb1 = __fsub_rn(1.0f, b1);
+    c.omb2 = __fsub_rn(1.0f, b2);
+    c.eps = eps;
+    c.wd = wd;
+    c.decay = __fmaf_rn(-lr, wd, 1.0f);
+    const float bc1 = __fsub_rn(1.0f, powf(b1, (float)step));
+    const float bc2 = __fsub_rn(1.0f, powf(b2, (float)step));
+    c.step_size = __fdiv_rn(lr, bc1);
+    c.sqrt_bc2 = __fsqrt_rn(bc2);
+    c.inv_sqrt_bc2 = __frcp_rn(c.sqrt_bc2);
+    c.lm_d = pow(2.0, m_bits - 1);
+    c.lv_d = pow(2.0, v_bits) - 1.0;
+    c.lm_f = (float)c.lm_d;
+    c.lv_f = (float)c.lv_d;
+    return c;
+}
+
+// Dequantised second moment: expf(q * sv + v_min)  (CUDA/stquant_kernel.cu:169).
+__device__ __forceinline__ float dequant_v(float q, float sv, float vmin) {
+    return expf(__fmaf_rn(q, sv, vmin));
+}
+
+// m = beta1*m + (1-beta1)*g  (CUDA/stquant_kernel.cu:175).
+__device__ __forceinline__ float adam_m(float m, float g, const StepConsts& c) {
+    return __fmaf_rn(c.b1, m, __fmul_rn(c.omb1, g));
+}
+
+// v = beta2*v + (1-beta2)*g*g  (CUDA/stquant_kernel.cu:176).
+__device__ __forceinline__ float adam_v(float v, float g, const StepConsts& c) {
+    return __fmaf_rn(c.b2, v, __fmul_rn(__fmul_rn(c.omb2, g), g));
+}
+
+// Parameter update with the unquantised moments (CUDA/stquant_kernel.cu:220-229).
+template <bool EXACT>
+__device__ __forceinline__ float update_p(float w, float m, float v, const StepConsts& c) {
+    if (EXACT) {
+        const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), c.sqrt_bc2), c.eps);
+        if (c.wd != 0.0f) w = __fmul_rn(w, c.decay);
+        return __fmaf_rn(-c.step_size, __fdiv_rn(m, denom), w);
+    } else {
+        // Hardware square root and reciprocal: a few ulp on the update term.
+        float s;
+        asm("sqrt.approx.f32 %0, %1;" : "=f"(s) : "f"(v));
+        const float denom = __fmaf_rn(s, c.inv_sqrt_bc2, c.eps);
+        if (c.wd != 0.0f) w = w * c.decay;
+        return __fmaf_rn(-c.step_size, __fdividef(m, denom), w);
+    }
+}
+
+// log(v + 1e-12)  (CUDA/stquant_kernel.cu:185).
+__device__ __forceinline__ float log_v_of(float v) { return logf(__fadd_rn(v, 1e-12f)); }
+
+// New block scales from the block reductions (CUDA/stquant_kernel.cu:192-195).
+__device__ __forceinline__ float scale_m_of(float max_abs_m, const StepConsts& c) {
+    return __fdiv_rn(__fadd_rn(max_abs_m, 1e-12f), c.lm_f);
+}
+__device__ __forceinline__ float scale_v_of(float max_lv, float min_lv, const StepConsts& c) {
+    return __fdiv_rn(__fadd_rn(__fsub_rn(max_lv, min_lv), 1e-12f), c.lv_f);
+}
+
+// ---------------------------------------------------------------------------
+// Requantisation.
+//
+// The reference computes q = round((double)x / (double)d) in double precision
+// (round = half away from zero) and clamps in double (CUDA/stquant_kernel.cu:
+// 205-215).  x and d are floats.  For |x/d| < 2^17 the double quotient never
+// lands on, or crosses, a half-integer that the exact quotient does not, since
+// a quotient of two floats that is not itself a half-integer stays at least
+// 2^-26 away from every half-integer, while the double rounding error is below
+// 2^-36; hence q = round_half_away(x/d) exactly.  The fast path computes
+// y = |x| * RN(1/d) (relative error < 2^-22.9) and accepts rint(y) when y lies
+// farther than y*2^-21 from the nearest half-integer; otherwise (and for NaN /
+// Inf) it evaluates the reference's double expression itself.  Both branches
+// therefore return the reference's code bit for bit.
+// ---------------------------------------------------------------------------
+
+// Reference expression for a signed (m) code, clamped to [-L, L-1].
+__device__ __noinline__ double requant_m_ref(float x, float d, double lm) {
+    double q = round((double)x / (double)d);
+    const double lo = -lm, hi = lm - 1.0;
+    if (q < lo) q = lo;
+    if (q > hi) q = hi;
+    return q;
+}
+
+// Reference expression for an unsigned (v) code, clamped to [0, L].
+__device__ __noinline__ double requant_v_ref(float x, float d, double lv) {
+    double q = round((double)x / (double)d);
+    if (q < 0.0) q = 0.0;
+    if (q > lv) q = lv;
+    return q;
+}
+
+// x/d rounded to an integer when provably equal to the double path (rounding
+// is symmetric, and exact ties never pass the test); sets `ok` otherwise.
+__device__ __forceinline__ float round_ratio_fast(float x, float rd, bool& ok) {
+    const float y = __fmul_rn(x, rd);
+    const float r = rintf(y);
+    const float t = fabsf(__fsub_rn(y, r));
+    ok = __fmaf_rn(fabsf(y), 0x1p-21f, t) < 0.5f;  // false for NaN / Inf as well
+    return r;
+}
+
+}  // namespace mdq

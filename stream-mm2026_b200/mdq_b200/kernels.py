@@ -1,0 +1,189 @@
+"""Torch-tensor front end of the C ABI.
+
+``fused_mdq_adamw`` keeps the exact argument list of the reference binding
+``stquant_timetest_cpp.fused_mdq_adamw`` (CUDA/stquant_core.cpp:3-15,
+CUDA/stquant_kernel.cu:414-465): it mutates p, the codes and the scales in
+place on the current stream and raises RuntimeError where the reference's
+TORCH_CHECKs would.  ``step_multi`` updates many tensors in one call.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import (LAYOUT_M8V4, LAYOUT_PACKED4, LAYOUT_S8U8, LAYOUT_S16U16, LAYOUT_S32U32,
+                   P_EXACT, P_FAST, StepOptions, TensorDesc)
+
+_DTYPE_CODE = {
+    torch.float32: _lib.MDQ_F32,
+    torch.bfloat16: _lib.MDQ_BF16,
+    torch.int8: _lib.MDQ_I8,
+    torch.uint8: _lib.MDQ_U8,
+    torch.int16: _lib.MDQ_I16,
+    torch.uint16: _lib.MDQ_U16,
+    torch.int32: _lib.MDQ_I32,
+    torch.uint32: _lib.MDQ_U32,
+}
+
+LAYOUT_NAMES = {
+    LAYOUT_PACKED4: "packed4",
+    LAYOUT_S8U8: "s8u8",
+    LAYOUT_S16U16: "s16u16",
+    LAYOUT_S32U32: "s32u32",
+    LAYOUT_M8V4: "m8v4",
+}
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    if t is None or t.numel() == 0:
+        return None
+    return t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _need_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} must be CUDA")
+
+
+def _need_contig(t: torch.Tensor, what: str) -> None:
+    if not t.is_contiguous():
+        raise RuntimeError(f"{what} must be contiguous")
+
+
+def fused_mdq_adamw(p, grad, exp_avg, exp_avg_sq, scale_m, scale_v, v_min,
+                    beta1, beta2, lr, weight_decay, eps, step, bits, block_size,
+                    profile_cycles=None):
+    """In-place fused MDQ-AdamW step of one tensor (reference argument list)."""
+    _need_cuda(p, "p/grad")
+    _need_cuda(grad, "p/grad")
+    _need_cuda(exp_avg, "exp_avg")
+    if p.dtype != torch.float32:
+        raise RuntimeError("p must be float32")
+    if grad.dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("grad must be float32 or bfloat16")
+    for t, name in ((p, "p"), (grad, "grad"), (exp_avg, "exp_avg"), (exp_avg_sq, "exp_avg_sq"),
+                    (scale_m, "scale_m"), (scale_v, "scale_v"), (v_min, "v_min")):
+        _need_contig(t, name)
+    if grad.numel() != p.numel():
+        raise RuntimeError("grad numel must match p")
+    prof = None
+    if profile_cycles is not None and profile_cycles.numel() > 0:
+        if not (profile_cycles.is_cuda and profile_cycles.dtype == torch.int64):
+            raise RuntimeError("profile_cycles must be CUDA int64 tensor")
+        if profile_cycles.numel() < 5:
+            raise RuntimeError("profile_cycles needs >= 5 elements")
+        prof = profile_cycles.data_ptr()
+    ea_code = _DTYPE_CODE.get(exp_avg.dtype, -1)
+    eas_code = _DTYPE_CODE.get(exp_avg_sq.dtype, -1)
+    lib = _lib.load()
+    with torch.cuda.device(p.device):
+        st = lib.mdq_fused_adamw(
+            p.data_ptr(), grad.data_ptr(), _DTYPE_CODE[grad.dtype],
+            _ptr(exp_avg), ea_code, exp_avg.numel(),
+            _ptr(exp_avg_sq), eas_code, exp_avg_sq.numel(),
+            scale_m.data_ptr(), scale_v.data_ptr(), v_min.data_ptr(),
+            p.numel(),
+            float(beta1), float(beta2), float(lr), float(weight_decay), float(eps),
+            int(step), int(bits), int(block_size), prof, _stream_handle(p.device))
+    _lib.check(st)
+
+
+@dataclass
+class StepItem:
+    """One tensor, or one block-aligned piece of a tensor, for ``step_multi``."""
+
+    p: torch.Tensor
+    grad: torch.Tensor
+    exp_avg: torch.Tensor
+    exp_avg_sq: Optional[torch.Tensor]
+    scale_m: torch.Tensor
+    scale_v: torch.Tensor
+    v_min: torch.Tensor
+    step: int
+    block: int
+    lr: float
+    weight_decay: float
+    eps: float
+    beta1: float
+    beta2: float
+    m_bits: int
+    v_bits: int
+    layout: int
+
+
+def fill_desc(d: TensorDesc, it: StepItem) -> None:
+    d.p = it.p.data_ptr()
+    d.grad = it.grad.data_ptr()
+    d.exp_avg = it.exp_avg.data_ptr()
+    d.exp_avg_sq = _ptr(it.exp_avg_sq)
+    d.scale_m = it.scale_m.data_ptr()
+    d.scale_v = it.scale_v.data_ptr()
+    d.v_min = it.v_min.data_ptr()
+    d.n = it.p.numel()
+    d.step = int(it.step)
+    d.block = int(it.block)
+    d.lr = float(it.lr)
+    d.weight_decay = float(it.weight_decay)
+    d.eps = float(it.eps)
+    d.beta1 = float(it.beta1)
+    d.beta2 = float(it.beta2)
+    d.m_bits = int(it.m_bits)
+    d.v_bits = int(it.v_bits)
+    d.layout = int(it.layout)
+    d.grad_dtype = _DTYPE_CODE.get(it.grad.dtype, -1)
+
+
+def run_descs(descs, count: int, device: torch.device, p_mode: int = P_FAST,
+              profile_cycles: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> None:
+    """Launch a prepared ``TensorDesc`` array (the optimizer keeps one alive)."""
+    opts = StepOptions(p_mode, profile_cycles.data_ptr() if profile_cycles is not None else None)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        st = lib.mdq_adamw_step_multi(descs, count, ctypes.byref(opts),
+                                      stream if stream is not None else _stream_handle(device))
+    _lib.check(st)
+
+
+def step_multi(items: Sequence[StepItem], p_mode: int = P_FAST,
+               profile_cycles: Optional[torch.Tensor] = None) -> None:
+    """Fused MDQ-AdamW step of many tensors on the current stream."""
+    if not items:
+        return
+    arr = (TensorDesc * len(items))()
+    dev = items[0].p.device
+    for d, it in zip(arr, items):
+        for t in (it.p, it.grad, it.exp_avg, it.scale_m, it.scale_v, it.v_min):
+            _need_cuda(t, "step tensors")
+            _need_contig(t, "step tensors")
+            if t.device != dev:
+                raise RuntimeError("all tensors of one step_multi call must share a device")
+        fill_desc(d, it)
+    run_descs(arr, len(items), dev, p_mode, profile_cycles)
+
+
+def layout_for_bits(m_bits: int, v_bits: int) -> int:
+    """Storage layout the optimizer uses for a (m_bits, v_bits) pair."""
+    if m_bits == v_bits:
+        if m_bits <= 4:
+            return LAYOUT_PACKED4
+        if m_bits <= 8:
+            return LAYOUT_S8U8
+        if m_bits <= 16:
+            return LAYOUT_S16U16
+        return LAYOUT_S32U32
+    if m_bits <= 8 and v_bits <= 4:
+        return LAYOUT_M8V4
+    b = max(m_bits, v_bits)
+    return layout_for_bits(b, b)
+
+
+__all__ = ["fused_mdq_adamw", "StepItem", "step_multi", "run_descs", "fill_desc",
+           "layout_for_bits", "P_FAST", "P_EXACT", "LAYOUT_NAMES"]
