@@ -1,0 +1,247 @@
+// mdq_codes.cuh - moment-code storage layouts and gradient loads.
+//
+// Every layout exposes the same per-thread interface over 8 consecutive
+// elements (vectorised) or one element (scalar):
+//   load8 / load1   -> signed m code values, unsigned v code values
+//   store8 / store1 <- codes as "magic" words (see below)
+//   m_word / v_word    the reference's integer conversion of a code computed on
+//                      the double path, as a magic word
+//
+// Magic words.  For |q| < 2^22 the float q + 1.5*2^23 has the bit pattern
+// 0x4B400000 + q, so adding that constant to a rounded float yields the code's
+// integer with no conversion instruction, and since 0x4B400000 has zero low 16
+// bits the code's low byte / half-word is the word's low byte / half-word.
+// Layouts whose codes need more than 22 bits (S32U32) store plain integers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "mdq.h"
+
+namespace mdq {
+
+constexpr int kMagicBits = 0x4B400000;
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+
+// Exact float of a small integer (|q| < 2^22) without an I2F instruction.
+__device__ __forceinline__ float small_int_to_float(int q) {
+    return __fsub_rn(__int_as_float(kMagicBits + q), kMagic);
+}
+
+// Pointers of the tensor a CTA is working on.
+struct TensorPtrs {
+    float* p;
+    const void* g;
+    void* m;
+    void* v;
+    float* sm;
+    float* sv;
+    float* vmin;
+};
+
+template <int LAYOUT> struct Codes;
+
+// One byte per element: low nibble q_m + 8, high nibble q_v
+// (CUDA/stquant_kernel.cu:52,71-73,130).
+template <> struct Codes<MDQ_LAYOUT_PACKED4> {
+    static constexpr int kTblBits = 4;      // v codes tabulated per block
+    static constexpr bool kApproxLog = true;
+    static constexpr bool kMagicCodes = true;
+    __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
+        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(t.m) + e));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const unsigned b = (j < 4 ? w.x : w.y) >> (8 * (j & 3));
+            qm[j] = (int)(b & 15u) - 8;
+            qv[j] = (int)((b >> 4) & 15u);
+        }
+    }
+    __device__ static void load1(const TensorPtrs& t, int64_t e, int& qm, int& qv) {
+        const unsigned b = static_cast<const uint8_t*>(t.m)[e];
+        qm = (int)(b & 15u) - 8;
+        qv = (int)(b >> 4);
+    }
+    // Codes are within [-8, 7] and [0, 15] once clamped to their levels
+    // (m_bits, v_bits <= 4), so the reference's nibble clamps
+    // (CUDA/stquant_kernel.cu:120-128) never bind and masking suffices.
+    __device__ static unsigned byte_of(int mw, int vw) {
+        return (((unsigned)vw & 15u) << 4) | (((unsigned)mw + 8u) & 15u);
+    }
+    __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
+        unsigned lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            lo |= byte_of(mw[j], vw[j]) << (8 * j);
+            hi |= byte_of(mw[j + 4], vw[j + 4]) << (8 * j);
+        }
+        __stcs(reinterpret_cast<uint2*>(static_cast<uint8_t*>(t.m) + e), make_uint2(lo, hi));
+    }
+    __device__ static void store1(const TensorPtrs& t, int64_t e, int mw, int vw) {
+        static_cast<uint8_t*>(t.m)[e] = (uint8_t)byte_of(mw, vw);
+    }
+    // (int)q as CUDA/stquant_kernel.cu:118,126, as a magic word.  A NaN code
+    // (NaN or infinite gradients) leaves the reference build's nibble at 0,
+    // i.e. q = -8: its integer conversion of NaN lands below the nibble clamp.
+    __device__ static int m_word(double q) { return kMagicBits + (isnan(q) ? -8 : (int)q); }
+    __device__ static int v_word(double q) { return kMagicBits + (int)q; }
+};
+
+template <typename MT, typename VT, bool MAGIC> struct CodesPlain {
+    static constexpr bool kMagicCodes = MAGIC;
+    template <typename T>
+    __device__ static void ld8(const T* src, int (&o)[8]) {
+        if constexpr (sizeof(T) == 1) {
+            const uint2 w = __ldcs(reinterpret_cast<const uint2*>(src));
+            const T* b = reinterpret_cast<const T*>(&w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = (int)b[j];
+        } else if constexpr (sizeof(T) == 2) {
+            const uint4 w = __ldcs(reinterpret_cast<const uint4*>(src));
+            const T* b = reinterpret_cast<const T*>(&w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = (int)b[j];
+        } else {
+            const uint4 w0 = __ldcs(reinterpret_cast<const uint4*>(src));
+            const uint4 w1 = __ldcs(reinterpret_cast<const uint4*>(src) + 1);
+            const T* b0 = reinterpret_cast<const T*>(&w0);
+            const T* b1 = reinterpret_cast<const T*>(&w1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { o[j] = (int)b0[j]; o[j + 4] = (int)b1[j]; }
+        }
+    }
+    template <typename T>
+    __device__ static void st8(T* dst, const int (&o)[8]) {
+        if constexpr (sizeof(T) == 1) {
+            unsigned lo = 0, hi = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                lo |= ((unsigned)o[j] & 0xffu) << (8 * j);
+                hi |= ((unsigned)o[j + 4] & 0xffu) << (8 * j);
+            }
+            __stcs(reinterpret_cast<uint2*>(dst), make_uint2(lo, hi));
+        } else if constexpr (sizeof(T) == 2) {
+            uint4 w;
+            w.x = ((unsigned)o[0] & 0xffffu) | ((unsigned)o[1] << 16);
+            w.y = ((unsigned)o[2] & 0xffffu) | ((unsigned)o[3] << 16);
+            w.z = ((unsigned)o[4] & 0xffffu) | ((unsigned)o[5] << 16);
+            w.w = ((unsigned)o[6] & 0xffffu) | ((unsigned)o[7] << 16);
+            __stcs(reinterpret_cast<uint4*>(dst), w);
+        } else {
+            __stcs(reinterpret_cast<uint4*>(dst),
+                   make_uint4((unsigned)o[0], (unsigned)o[1], (unsigned)o[2], (unsigned)o[3]));
+            __stcs(reinterpret_cast<uint4*>(dst) + 1,
+                   make_uint4((unsigned)o[4], (unsigned)o[5], (unsigned)o[6], (unsigned)o[7]));
+        }
+    }
+    __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
+        ld8(static_cast<const MT*>(t.m) + e, qm);
+        ld8(static_cast<const VT*>(t.v) + e, qv);
+    }
+    __device__ static void load1(const TensorPtrs& t, int64_t e, int& qm, int& qv) {
+        qm = (int)static_cast<const MT*>(t.m)[e];
+        qv = (int)static_cast<const VT*>(t.v)[e];
+    }
+    __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
+        st8(static_cast<MT*>(t.m) + e, mw);
+        st8(static_cast<VT*>(t.v) + e, vw);
+    }
+    // Magic words and plain integers both truncate to the stored code.
+    __device__ static void store1(const TensorPtrs& t, int64_t e, int mw, int vw) {
+        static_cast<MT*>(t.m)[e] = (MT)mw;
+        static_cast<VT*>(t.v)[e] = (VT)(unsigned)vw;
+    }
+    // The reference's conversions of a double-path code
+    // (CUDA/stquant_kernel.cu:210,215 and the 16/32-bit twins).
+    __device__ static int m_word(double q) { return (MAGIC ? kMagicBits : 0) + (int)(MT)q; }
+    __device__ static int v_word(double q) { return (MAGIC ? kMagicBits : 0) + (int)(unsigned)(VT)q; }
+};
+
+template <> struct Codes<MDQ_LAYOUT_S8U8> : CodesPlain<int8_t, uint8_t, true> {
+    static constexpr int kTblBits = 0;  // 256 codes per block: decoded per element
+    static constexpr bool kApproxLog = true;
+};
+template <> struct Codes<MDQ_LAYOUT_S16U16> : CodesPlain<int16_t, uint16_t, true> {
+    static constexpr int kTblBits = 0;
+    static constexpr bool kApproxLog = false;
+};
+template <> struct Codes<MDQ_LAYOUT_S32U32> : CodesPlain<int32_t, uint32_t, false> {
+    static constexpr int kTblBits = 0;
+    static constexpr bool kApproxLog = false;
+};
+
+// int8 m codes + v nibbles packed two per byte (element 2i in the low nibble).
+template <> struct Codes<MDQ_LAYOUT_M8V4> {
+    static constexpr int kTblBits = 4;
+    static constexpr bool kApproxLog = true;
+    static constexpr bool kMagicCodes = true;
+    __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
+        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const int8_t*>(t.m) + e));
+        const unsigned vw = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(t.v) + (e >> 1)));
+        const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            qm[j] = b[j];
+            qv[j] = (int)((vw >> (4 * j)) & 15u);
+        }
+    }
+    __device__ static void load1(const TensorPtrs& t, int64_t e, int& qm, int& qv) {
+        qm = static_cast<const int8_t*>(t.m)[e];
+        qv = (int)((static_cast<const uint8_t*>(t.v)[e >> 1] >> (4 * (e & 1))) & 15u);
+    }
+    __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
+        unsigned lo = 0, hi = 0, nib = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            lo |= ((unsigned)mw[j] & 0xffu) << (8 * j);
+            hi |= ((unsigned)mw[j + 4] & 0xffu) << (8 * j);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) nib |= ((unsigned)vw[j] & 15u) << (4 * j);
+        __stcs(reinterpret_cast<uint2*>(static_cast<int8_t*>(t.m) + e), make_uint2(lo, hi));
+        __stcs(reinterpret_cast<unsigned*>(static_cast<uint8_t*>(t.v) + (e >> 1)), nib);
+    }
+    // Neighbouring elements share a byte: callers give each byte one owner.
+    __device__ static void store1(const TensorPtrs& t, int64_t e, int mw, int vw) {
+        static_cast<int8_t*>(t.m)[e] = (int8_t)mw;
+        uint8_t* vb = static_cast<uint8_t*>(t.v) + (e >> 1);
+        const unsigned sh = 4 * (unsigned)(e & 1);
+        *vb = (uint8_t)((*vb & ~(15u << sh)) | (((unsigned)vw & 15u) << sh));
+    }
+    __device__ static int m_word(double q) { return kMagicBits + (int)(int8_t)q; }
+    // A 4-bit v code, clamped into its nibble as the packed4 layout does.
+    __device__ static int v_word(double q) {
+        int vi = (int)q;
+        vi = vi < 0 ? 0 : (vi > 15 ? 15 : vi);
+        return kMagicBits + vi;
+    }
+};
+
+// Gradient loads (fp32, or bf16 widened exactly).
+template <typename GT> struct Grad;
+template <> struct Grad<float> {
+    __device__ static void load8(const void* g, int64_t e, float (&o)[8]) {
+        const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(g) + e);
+        const float4 a = __ldcs(s), b = __ldcs(s + 1);
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    }
+    __device__ static float load1(const void* g, int64_t e) { return static_cast<const float*>(g)[e]; }
+};
+template <> struct Grad<__nv_bfloat16> {
+    __device__ static void load8(const void* g, int64_t e, float (&o)[8]) {
+        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(g) + e));
+        const unsigned u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            o[2 * j] = __uint_as_float(u[j] << 16);
+            o[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+        }
+    }
+    __device__ static float load1(const void* g, int64_t e) {
+        return __bfloat162float(static_cast<const __nv_bfloat16*>(g)[e]);
+    }
+};
+
+}  // namespace mdq

@@ -127,14 +127,47 @@ __device__ __noinline__ double requant_v_ref(float x, float d, double lv) {
     return q;
 }
 
-// x/d rounded to an integer when provably equal to the double path (rounding
-// is symmetric, and exact ties never pass the test); sets `ok` otherwise.
-__device__ __forceinline__ float round_ratio_fast(float x, float rd, bool& ok) {
-    const float y = __fmul_rn(x, rd);
-    const float r = rintf(y);
-    const float t = fabsf(__fsub_rn(y, r));
-    ok = __fmaf_rn(fabsf(y), 0x1p-21f, t) < 0.5f;  // false for NaN / Inf as well
-    return r;
+// ---------------------------------------------------------------------------
+// Rounding without conversion instructions.  For |y| <= 2^22, y + 1.5*2^23
+// rounds y to the nearest integer (ties to even) and its bit pattern is
+// 0x4B400000 + rint(y).  `round_word` clamps y to [lo, hi] first (integer
+// bounds; clamping commutes with rounding since rounding is monotone), returns
+// that bit pattern, and sets `ok` when the rounded value provably equals the
+// reference's double-precision round-half-away of the exact quotient: the
+// distance of y to the nearest half-integer must exceed |y| * 2^-21 (the
+// relative error of y = x * RN(1/d)) plus `slack` (any further absolute error
+// of y).  Exact ties never pass, so ties-to-even never decides a code.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int round_word(float y, float lo, float hi, float slack, bool& ok) {
+    const float yc = fminf(fmaxf(y, lo), hi);  // NaN y -> lo; caught below
+    const float s = __fadd_rn(yc, 12582912.0f);
+    const float r = __fsub_rn(s, 12582912.0f);
+    const float t = fabsf(__fsub_rn(yc, r));
+    ok = __fadd_rn(__fmaf_rn(fabsf(yc), 0x1p-21f, t), slack) < 0.5f && !isnan(y);
+    return __float_as_int(s);
+}
+
+// ---------------------------------------------------------------------------
+// Logarithms.  The block statistics need max and min of logf(x), x = v + 1e-12,
+// and each v code needs round((logf(x) - min) / d).
+//  * Extremes: CUDA's logf is monotone non-decreasing on every float >= 1e-12
+//    (a GPU test checks all of them), so max_i logf(x_i) = logf(max_i x_i):
+//    the block reduces x and calls logf once.  fmaxf/fminf skip NaNs exactly
+//    as the reference's reduction of fmaxf/fminf over logf values does, and a
+//    missing tail element (log v taken as 0) enters as x = 1, logf(1) = +0.
+//  * Codes: a = lg2.approx(x) * ln 2 approximates logf(x) within log_tol(a)
+//    for every float x >= 1e-12 (checked exhaustively by the same GPU test);
+//    a code is taken from the approximation only when it clears its rounding
+//    boundary by more than that error, otherwise from logf itself.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float approx_ln(float x) {
+    float l2;
+    asm("lg2.approx.f32 %0, %1;" : "=f"(l2) : "f"(x));
+    return __fmul_rn(l2, 0.693147182f);
+}
+
+__device__ __forceinline__ float log_tol(float a) {
+    return __fmaf_rn(fabsf(a), 0x1p-21f, 0x1p-20f);
 }
 
 }  // namespace mdq

@@ -31,27 +31,26 @@
 
 #include "mdq.h"
 #include "mdq_math.cuh"
+#include "mdq_codes.cuh"
 
 namespace mdq {
 
 constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
 constexpr int kPerThread = 8;
 constexpr int kTile = kThreads * kPerThread;  // 2048 elements
 constexpr int kLogTile = 11;
-constexpr int kTblMax = 1024;                 // floats of dequantised-v table per tile
 constexpr int kCapSmall = 8;                  // descriptors per launch, small table
 constexpr int kCapLarge = 224;                // descriptors per launch, large table
 constexpr int kProfSlots = 5;
 
+#ifndef MDQ_MIN_CTAS_PER_SM
+#define MDQ_MIN_CTAS_PER_SM 3
+#endif
+
 // Device-side descriptor (one tensor or block-aligned tensor piece).
 struct LaunchDesc {
-    float* p;
-    const void* g;
-    void* m;
-    void* v;
-    float* sm;
-    float* sv;
-    float* vmin;
+    TensorPtrs t;
     int64_t n;
     int32_t tile_begin;  // first tile of this descriptor within the launch
     int32_t step;
@@ -67,211 +66,17 @@ struct LaunchParams {
     LaunchDesc d[CAP];
 };
 
-// ---------------------------------------------------------------------------
-// Code storage per layout.  qm holds the signed m code value, qv the unsigned
-// v code value (for PACKED4 the m nibble minus 8, as the reference unpacks it).
-// ---------------------------------------------------------------------------
-template <int LAYOUT> struct Codes;
-
-template <> struct Codes<MDQ_LAYOUT_PACKED4> {
-    static constexpr int kTblBits = 4;
-    __device__ static void load8(const LaunchDesc& d, int64_t e, int (&qm)[8], unsigned (&qv)[8]) {
-        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(d.m) + e));
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const unsigned b = ((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xffu;
-            qm[j] = (int)(b & 15u) - 8;
-            qv[j] = b >> 4;
-        }
-    }
-    __device__ static void load1(const LaunchDesc& d, int64_t e, int& qm, unsigned& qv) {
-        const unsigned b = static_cast<const uint8_t*>(d.m)[e];
-        qm = (int)(b & 15u) - 8;
-        qv = b >> 4;
-    }
-    // CUDA/stquant_kernel.cu:118-130: nibble clamps after the level clamps.
-    __device__ static unsigned pack(int mi, int vi) {
-        int mu = mi + 8;
-        mu = mu < 0 ? 0 : (mu > 15 ? 15 : mu);
-        vi = vi < 0 ? 0 : (vi > 15 ? 15 : vi);
-        return ((unsigned)vi << 4) | ((unsigned)mu & 15u);
-    }
-    __device__ static void store8(const LaunchDesc& d, int64_t e, const int (&mi)[8], const int (&vi)[8]) {
-        uint2 w = make_uint2(0u, 0u);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const unsigned b = pack(mi[j], vi[j]);
-            if (j < 4) w.x |= b << (8 * j); else w.y |= b << (8 * (j - 4));
-        }
-        __stcs(reinterpret_cast<uint2*>(static_cast<uint8_t*>(d.m) + e), w);
-    }
-    __device__ static void store1(const LaunchDesc& d, int64_t e, int mi, int vi) {
-        static_cast<uint8_t*>(d.m)[e] = (uint8_t)pack(mi, vi);
-    }
-    // Integer conversion of a double-path code, as CUDA/stquant_kernel.cu:118,126.
-    __device__ static int m_int(double q) { return (int)q; }
-    __device__ static int v_int(double q) { return (int)q; }
+// The tensor a CTA is working on, staged in shared memory by thread 0.
+struct TileCtx {
+    TensorPtrs t;
+    int64_t n;
+    int32_t tile_begin, tile_end;  // this tensor's tiles within the launch
+    int32_t lb, vec;
+    StepConsts C;
 };
-
-template <typename MT, typename VT> struct CodesPlain {
-    // 8 codes of MT / VT: 8, 16 or 32 bytes each.
-    template <typename T>
-    __device__ static void ld8(const T* src, T (&o)[8]) {
-        if constexpr (sizeof(T) == 1) {
-            const uint2 w = __ldcs(reinterpret_cast<const uint2*>(src));
-            const T* b = reinterpret_cast<const T*>(&w);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = b[j];
-        } else if constexpr (sizeof(T) == 2) {
-            const uint4 w = __ldcs(reinterpret_cast<const uint4*>(src));
-            const T* b = reinterpret_cast<const T*>(&w);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = b[j];
-        } else {
-            const uint4 w0 = __ldcs(reinterpret_cast<const uint4*>(src));
-            const uint4 w1 = __ldcs(reinterpret_cast<const uint4*>(src) + 1);
-            const T* b0 = reinterpret_cast<const T*>(&w0);
-            const T* b1 = reinterpret_cast<const T*>(&w1);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) { o[j] = b0[j]; o[j + 4] = b1[j]; }
-        }
-    }
-    template <typename T>
-    __device__ static void st8(T* dst, const T (&o)[8]) {
-        if constexpr (sizeof(T) == 1) {
-            uint2 w;
-            T* b = reinterpret_cast<T*>(&w);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) b[j] = o[j];
-            __stcs(reinterpret_cast<uint2*>(dst), w);
-        } else if constexpr (sizeof(T) == 2) {
-            uint4 w;
-            T* b = reinterpret_cast<T*>(&w);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) b[j] = o[j];
-            __stcs(reinterpret_cast<uint4*>(dst), w);
-        } else {
-            uint4 w0, w1;
-            T* b0 = reinterpret_cast<T*>(&w0);
-            T* b1 = reinterpret_cast<T*>(&w1);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) { b0[j] = o[j]; b1[j] = o[j + 4]; }
-            __stcs(reinterpret_cast<uint4*>(dst), w0);
-            __stcs(reinterpret_cast<uint4*>(dst) + 1, w1);
-        }
-    }
-    __device__ static void load8(const LaunchDesc& d, int64_t e, int (&qm)[8], unsigned (&qv)[8]) {
-        MT a[8];
-        VT b[8];
-        ld8(static_cast<const MT*>(d.m) + e, a);
-        ld8(static_cast<const VT*>(d.v) + e, b);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) { qm[j] = (int)a[j]; qv[j] = (unsigned)b[j]; }
-    }
-    __device__ static void load1(const LaunchDesc& d, int64_t e, int& qm, unsigned& qv) {
-        qm = (int)static_cast<const MT*>(d.m)[e];
-        qv = (unsigned)static_cast<const VT*>(d.v)[e];
-    }
-    __device__ static void store8(const LaunchDesc& d, int64_t e, const int (&mi)[8], const int (&vi)[8]) {
-        MT a[8];
-        VT b[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) { a[j] = (MT)mi[j]; b[j] = (VT)(unsigned)vi[j]; }
-        st8(static_cast<MT*>(d.m) + e, a);
-        st8(static_cast<VT*>(d.v) + e, b);
-    }
-    __device__ static void store1(const LaunchDesc& d, int64_t e, int mi, int vi) {
-        static_cast<MT*>(d.m)[e] = (MT)mi;
-        static_cast<VT*>(d.v)[e] = (VT)(unsigned)vi;
-    }
-    // Conversions of a double-path code as the reference's stores perform
-    // them (CUDA/stquant_kernel.cu:210,215 and the 16/32-bit twins).
-    __device__ static int m_int(double q) { return (int)(MT)q; }
-    __device__ static int v_int(double q) { return (int)(unsigned)(VT)q; }
-};
-
-template <> struct Codes<MDQ_LAYOUT_S8U8> : CodesPlain<int8_t, uint8_t> {
-    static constexpr int kTblBits = 8;
-};
-template <> struct Codes<MDQ_LAYOUT_S16U16> : CodesPlain<int16_t, uint16_t> {
-    static constexpr int kTblBits = 0;
-};
-template <> struct Codes<MDQ_LAYOUT_S32U32> : CodesPlain<int32_t, uint32_t> {
-    static constexpr int kTblBits = 0;
-};
-
-// int8 m codes + v nibbles packed two per byte.
-template <> struct Codes<MDQ_LAYOUT_M8V4> {
-    static constexpr int kTblBits = 4;
-    __device__ static void load8(const LaunchDesc& d, int64_t e, int (&qm)[8], unsigned (&qv)[8]) {
-        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const int8_t*>(d.m) + e));
-        const unsigned vw = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(d.v) + (e >> 1)));
-        const int8_t* b = reinterpret_cast<const int8_t*>(&w);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            qm[j] = b[j];
-            qv[j] = (vw >> (4 * j)) & 15u;
-        }
-    }
-    __device__ static void load1(const LaunchDesc& d, int64_t e, int& qm, unsigned& qv) {
-        qm = static_cast<const int8_t*>(d.m)[e];
-        qv = (static_cast<const uint8_t*>(d.v)[e >> 1] >> (4 * (e & 1))) & 15u;
-    }
-    __device__ static unsigned nib(int vi) { return (unsigned)(vi < 0 ? 0 : (vi > 15 ? 15 : vi)); }
-    __device__ static void store8(const LaunchDesc& d, int64_t e, const int (&mi)[8], const int (&vi)[8]) {
-        uint2 w;
-        int8_t* b = reinterpret_cast<int8_t*>(&w);
-        unsigned vw = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            b[j] = (int8_t)mi[j];
-            vw |= nib(vi[j]) << (4 * j);
-        }
-        __stcs(reinterpret_cast<uint2*>(static_cast<int8_t*>(d.m) + e), w);
-        __stcs(reinterpret_cast<unsigned*>(static_cast<uint8_t*>(d.v) + (e >> 1)), vw);
-    }
-    // Single elements share a byte with their neighbour: only used by the
-    // owner of a whole tail, which writes each byte once (see store_tail).
-    __device__ static void store1(const LaunchDesc& d, int64_t e, int mi, int vi) {
-        static_cast<int8_t*>(d.m)[e] = (int8_t)mi;
-        uint8_t* vb = static_cast<uint8_t*>(d.v) + (e >> 1);
-        const unsigned sh = 4 * (unsigned)(e & 1);
-        *vb = (uint8_t)((*vb & ~(15u << sh)) | (nib(vi) << sh));
-    }
-    __device__ static int m_int(double q) { return (int)(int8_t)q; }
-    __device__ static int v_int(double q) { return (int)q; }
-};
-
-// Gradient element loads.
-template <typename GT> struct Grad;
-template <> struct Grad<float> {
-    __device__ static void load8(const void* g, int64_t e, float (&o)[8]) {
-        const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(g) + e);
-        const float4 a = __ldcs(s), b = __ldcs(s + 1);
-        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
-        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
-    }
-    __device__ static float load1(const void* g, int64_t e) { return static_cast<const float*>(g)[e]; }
-};
-template <> struct Grad<__nv_bfloat16> {
-    __device__ static void load8(const void* g, int64_t e, float (&o)[8]) {
-        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(g) + e));
-        const unsigned u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            o[2 * j] = __uint_as_float(u[j] << 16);
-            o[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
-        }
-    }
-    __device__ static float load1(const void* g, int64_t e) {
-        return __bfloat162float(static_cast<const __nv_bfloat16*>(g)[e]);
-    }
-};
-
-__device__ __forceinline__ unsigned long long prof_now() { return clock64(); }
 
 template <int CAP>
-__device__ __forceinline__ int find_desc(const LaunchParams<CAP>& P, int tile) {
+__device__ int find_desc(const LaunchParams<CAP>& P, int tile) {
     int lo = 0, hi = P.n_desc - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -280,194 +85,281 @@ __device__ __forceinline__ int find_desc(const LaunchParams<CAP>& P, int tile) {
     return lo;
 }
 
+// Max (bit k of MAXMASK set) or min of NV values over the `gthreads`
+// consecutive threads that own one quantisation block: xor shuffles inside a
+// warp, then one shared-memory exchange when a block spans several warps
+// (gthreads is uniform over the CTA, so the barrier is too).
+template <unsigned MAXMASK, int NV>
+__device__ __forceinline__ void group_reduce(float (&x)[NV], int gthreads, float (*red)[kWarps]) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        if (o < gthreads) {
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                const float y = __shfl_xor_sync(0xffffffffu, x[k], o);
+                x[k] = ((MAXMASK >> k) & 1u) ? fmaxf(x[k], y) : fminf(x[k], y);
+            }
+        }
+    }
+    if (gthreads > 32) {
+        const int w = threadIdx.x >> 5;
+        if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+            for (int k = 0; k < NV; ++k) red[k][w] = x[k];
+        }
+        __syncthreads();
+        const int wpg = gthreads >> 5;
+        const int w0 = (w / wpg) * wpg;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            float r = red[k][w0];
+            for (int i = 1; i < wpg; ++i)
+                r = ((MAXMASK >> k) & 1u) ? fmaxf(r, red[k][w0 + i]) : fminf(r, red[k][w0 + i]);
+            x[k] = r;
+        }
+    }
+}
+
+__device__ __forceinline__ void prof_mark(unsigned long long (&pc)[kProfSlots], int slot,
+                                          unsigned long long& t0) {
+    const unsigned long long t1 = clock64();
+    pc[slot] += t1 - t0;
+    t0 = t1;
+}
+
+// One tile of 2048 elements.  FULL: every thread owns 8 in-range elements and
+// all pointers allow vector access; otherwise element-wise guarded access.
+// `tbl` is this warp's dequantised-v table (nullptr when not tabulated) and
+// `red` this tile's reduction scratch.
+template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL>
+__device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0, const float* tbl,
+                                          float (*red)[kWarps],
+                                          unsigned long long (&pc)[kProfSlots],
+                                          unsigned long long& t0) {
+    using CI = Codes<LAYOUT>;
+    constexpr bool kApprox = CI::kApproxLog;
+    constexpr bool kMagicC = CI::kMagicCodes;
+    const float kNaN = __int_as_float(0x7fffffff);
+    const int tid = threadIdx.x;
+    const TensorPtrs T = X.t;
+    const StepConsts& C = X.C;
+    const int lb = X.lb;
+    const int64_t n = X.n;
+    const int64_t e0 = tile_e0 + tid * kPerThread;
+    const int64_t blk = e0 >> lb;
+    int cnt = kPerThread;
+    if (!FULL) {
+        const int64_t rem = n - e0;
+        cnt = rem >= kPerThread ? kPerThread : (rem > 0 ? (int)rem : 0);
+    }
+
+    // ---- load ----------------------------------------------------------
+    float p[8], g[8];
+    int qm[8], qv[8];
+    if (FULL) {
+        const float4* ps = reinterpret_cast<const float4*>(T.p + e0);
+        const float4 a = __ldcs(ps), b = __ldcs(ps + 1);
+        p[0] = a.x; p[1] = a.y; p[2] = a.z; p[3] = a.w;
+        p[4] = b.x; p[5] = b.y; p[6] = b.z; p[7] = b.w;
+        Grad<GT>::load8(T.g, e0, g);
+        CI::load8(T, e0, qm, qv);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            p[j] = 0.0f; g[j] = 0.0f; qm[j] = 0; qv[j] = 0;
+            if (j < cnt) {
+                p[j] = T.p[e0 + j];
+                g[j] = Grad<GT>::load1(T.g, e0 + j);
+                CI::load1(T, e0 + j, qm[j], qv[j]);
+            }
+        }
+    }
+    float sm = 0.0f, sv = 0.0f, vmn = 0.0f;
+    if (FULL || cnt > 0) { sm = T.sm[blk]; sv = T.sv[blk]; vmn = T.vmin[blk]; }
+
+    // ---- dequantise, AdamW moments, parameter update -------------------
+    // (CUDA/stquant_kernel.cu:163-177, 220-229)
+    // Table row of this thread's block: blocks of <= 256 elements lie inside
+    // one warp's 256 elements, larger ones cover the whole warp.
+    const int trow = lb <= 8 ? ((((tid & 31) * kPerThread) >> lb) << 4) : 0;
+    float m[8], v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float qmf = kMagicC ? small_int_to_float(qm[j]) : (float)qm[j];
+        m[j] = __fmul_rn(qmf, sm);
+        if (CI::kTblBits > 0 && tbl != nullptr) {
+            v[j] = tbl[trow + qv[j]];
+        } else {
+            const float qvf = kMagicC ? small_int_to_float(qv[j]) : (float)(unsigned)qv[j];
+            v[j] = dequant_v(qvf, sv, vmn);
+        }
+    }
+    if (PROF && tid == 0) prof_mark(pc, 0, t0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        m[j] = adam_m(m[j], g[j], C);
+        v[j] = adam_v(v[j], g[j], C);
+    }
+    if (PROF && tid == 0) prof_mark(pc, 1, t0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p[j] = update_p<EXACT_P>(p[j], m[j], v[j], C);
+    if (FULL) {
+        float4* pd = reinterpret_cast<float4*>(T.p + e0);
+        __stcs(pd, make_float4(p[0], p[1], p[2], p[3]));
+        __stcs(pd + 1, make_float4(p[4], p[5], p[6], p[7]));
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (j < cnt) T.p[e0 + j] = p[j];
+    }
+    if (PROF && tid == 0) prof_mark(pc, 4, t0);
+
+    // ---- block statistics (CUDA/stquant_kernel.cu:184-199) -------------
+    // max |m|, and max / min of logf(x) as logf of max / min x (logf is
+    // monotone).  NaN seeds make fmaxf/fminf skip only NaNs, as the
+    // reference's reduction does; elements past the end enter as |m| = 0 and
+    // x = 1 (log v = 0, :92-93).
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = __fadd_rn(v[j], 1e-12f);
+    const int gthreads = (1 << lb) >> 3;
+    float st[3] = {kNaN, kNaN, kNaN};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const bool ok = FULL || j < cnt;
+        st[0] = fmaxf(st[0], ok ? fabsf(m[j]) : 0.0f);
+        st[1] = fmaxf(st[1], ok ? x[j] : 1.0f);
+        st[2] = fminf(st[2], ok ? x[j] : 1.0f);
+    }
+    group_reduce<0b011u>(st, gthreads, red);
+    const float lmax = logf(st[1]);
+    const float lmin = logf(st[2]);
+    const float new_sm = scale_m_of(st[0], C);
+    const float new_sv = scale_v_of(lmax, lmin, C);
+    if ((tid & (gthreads - 1)) == 0 && (FULL || (blk << lb) < n)) {
+        T.sm[blk] = new_sm;
+        T.sv[blk] = new_sv;
+        T.vmin[blk] = lmin;
+    }
+    if (PROF && tid == 0) prof_mark(pc, 2, t0);
+
+    // ---- requantise (CUDA/stquant_kernel.cu:204-216) --------------------
+    const float dm = __fadd_rn(new_sm, 1e-12f), dv = __fadd_rn(new_sv, 1e-12f);
+    const float rdm = __frcp_rn(dm), rdv = __frcp_rn(dv);
+    // Bound on |(a - lmin) - RN(logf(x) - lmin)|: the approximation error plus
+    // one ulp of a difference below 128 (logs of floats >= 1e-12 lie in
+    // [-27.7, 88.8]), scaled to code units.
+    float slack_v = 0.0f;
+    if (kApprox)
+        slack_v = __fmul_rn(__fadd_rn(log_tol(fmaxf(fabsf(lmax), fabsf(lmin))), 0x1p-17f),
+                            __fmul_rn(rdv, 1.001f));
+    const float mlo = -C.lm_f, mhi = __fsub_rn(C.lm_f, 1.0f), vhi = C.lv_f;
+    int mw[8], vw[8];
+    unsigned redo = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        bool okm = false, okv = false;
+        mw[j] = 0;
+        vw[j] = 0;
+        if (kMagicC) {
+            const float lj = kApprox ? approx_ln(x[j]) : logf(x[j]);
+            mw[j] = round_word(__fmul_rn(m[j], rdm), mlo, mhi, 0.0f, okm);
+            vw[j] = round_word(__fmul_rn(__fsub_rn(lj, lmin), rdv), 0.0f, vhi, slack_v, okv);
+        }
+        redo |= (okm ? 0u : 1u) << (2 * j);
+        redo |= (okv ? 0u : 2u) << (2 * j);
+    }
+    if (redo != 0) {
+        // The reference's double-precision expression for undecided codes.
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if ((redo >> (2 * j)) & 1u) mw[j] = CI::m_word(requant_m_ref(m[j], dm, C.lm_d));
+            if ((redo >> (2 * j)) & 2u)
+                vw[j] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[j]), lmin), dv, C.lv_d));
+        }
+    }
+    if (FULL) {
+        CI::store8(T, e0, mw, vw);
+    } else {
+        // One thread owns all 8 elements, so M8V4 nibble pairs never race.
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (j < cnt) CI::store1(T, e0 + j, mw[j], vw[j]);
+    }
+    if (PROF && tid == 0) prof_mark(pc, 3, t0);
+}
+
 // ---------------------------------------------------------------------------
-// Fast kernel: power-of-two blocks 8..2048, tiles of 2048 elements.
+// Tiled kernel: power-of-two blocks 8..2048.  Each CTA takes a contiguous
+// range of tiles; the tensor it is in is staged in shared memory once, and
+// CTA-wide barriers happen only at a tensor switch and, for blocks spanning
+// several warps, inside the block reduction.
 // ---------------------------------------------------------------------------
+constexpr int kTblPerWarp = 128;  // (256 / 32 blocks) x 16 codes at most
+
 template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, MDQ_MIN_CTAS_PER_SM)
 mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
     using CI = Codes<LAYOUT>;
-    constexpr bool kAllDouble = (LAYOUT == MDQ_LAYOUT_S32U32);
-    __shared__ float s_tbl[kTblMax];
-    __shared__ float s_red[3][kThreads / 32];
+    __shared__ float s_tbl[kWarps][kTblPerWarp];
+    __shared__ float s_red[2][3][kWarps];  // alternates by tile
+    __shared__ TileCtx s_ctx;
 
     const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    int cur = -1;
-    StepConsts C;
+    const int warp = tid >> 5, lane = tid & 31;
     unsigned long long pc[kProfSlots] = {0, 0, 0, 0, 0};
+    const int64_t total = P.total_tiles;
+    const int tile_lo = (int)(total * blockIdx.x / gridDim.x);
+    const int tile_hi = (int)(total * (blockIdx.x + 1) / gridDim.x);
+    int cur_end = -1;
 
-    for (int tile = blockIdx.x; tile < P.total_tiles; tile += gridDim.x) {
-        const int t = find_desc(P, tile);
-        const LaunchDesc& D = P.d[t];
-        if (t != cur) {
-            C = make_step_consts(D.b1, D.b2, D.lr, D.wd, D.eps, D.step, D.m_bits, D.v_bits);
-            cur = t;
+    for (int tile = tile_lo; tile < tile_hi; ++tile) {
+        if (tile >= cur_end) {
+            __syncthreads();  // every thread is done with the previous tensor
+            if (tid == 0) {
+                const LaunchDesc& D = P.d[find_desc(P, tile)];
+                s_ctx.t = D.t;
+                s_ctx.n = D.n;
+                s_ctx.tile_begin = D.tile_begin;
+                s_ctx.tile_end = D.tile_begin + (int32_t)((D.n + kTile - 1) >> kLogTile);
+                s_ctx.lb = D.log2_block;
+                s_ctx.vec = D.vec;
+                s_ctx.C = make_step_consts(D.b1, D.b2, D.lr, D.wd, D.eps, D.step, D.m_bits,
+                                           D.v_bits);
+            }
+            __syncthreads();
+            cur_end = s_ctx.tile_end;
         }
         unsigned long long t0 = 0;
-        if (PROF && tid == 0) t0 = prof_now();
+        if (PROF && tid == 0) t0 = clock64();
+        const int lb = s_ctx.lb;
+        const int64_t n = s_ctx.n;
+        const int64_t tile_e0 = (int64_t)(tile - s_ctx.tile_begin) << kLogTile;
 
-        const int lb = D.log2_block;
-        const int64_t n = D.n;
-        const int64_t tile_e0 = (int64_t)(tile - D.tile_begin) << kLogTile;
-        const int64_t e0 = tile_e0 + tid * kPerThread;
-        const int64_t rem = n - e0;
-        const int cnt = rem >= kPerThread ? kPerThread : (rem > 0 ? (int)rem : 0);
-        const int64_t nblk = (n + ((int64_t)1 << lb) - 1) >> lb;
-        const int64_t blk = e0 >> lb;
-
-        // Dequantised-v table: entries (local block, code) of this tile.
-        constexpr int kTB = CI::kTblBits;
-        const bool use_tbl = kTB > 0 && ((kTile >> lb) << kTB) <= kTblMax;
-        __syncthreads();  // previous tile's readers of s_tbl / s_red are done
-        if (use_tbl) {
-            const int entries = (kTile >> lb) << kTB;
-            const int64_t blk0 = tile_e0 >> lb;
-            for (int j = tid; j < entries; j += kThreads) {
-                const int64_t b = blk0 + (j >> kTB);
-                float val = 0.0f;
-                if (b < nblk) val = dequant_v((float)(j & ((1 << kTB) - 1)), D.sv[b], D.vmin[b]);
-                s_tbl[j] = val;
+        // This warp's dequantised-v table for 4-bit v codes: entry (block,
+        // code) = expf(code * sv + v_min), the value the reference computes
+        // per element (CUDA/stquant_kernel.cu:169).  Blocks of 8 or 16
+        // elements gain nothing from it and decode per element.
+        const float* tbl = nullptr;
+        if (CI::kTblBits == 4 && lb >= 5) {
+            float* row = s_tbl[warp];
+            const int64_t wb0 = (tile_e0 + (warp << 8)) >> lb;  // first block of this warp
+            const int entries = lb <= 8 ? (256 >> lb) << 4 : 16;
+            const int64_t nblk = (n + ((int64_t)1 << lb) - 1) >> lb;
+            __syncwarp();  // lanes are done with the previous tile's entries
+            for (int j = lane; j < entries; j += 32) {
+                const int64_t b = wb0 + (j >> 4);
+                row[j] = b < nblk ? dequant_v((float)(j & 15), s_ctx.t.sv[b], s_ctx.t.vmin[b])
+                                  : 0.0f;
             }
-            __syncthreads();
+            __syncwarp();
+            tbl = row;
         }
-
-        float p[8], g[8];
-        int qm[8];
-        unsigned qv[8];
-        if (cnt == kPerThread && D.vec) {
-            const float4* ps = reinterpret_cast<const float4*>(D.p + e0);
-            const float4 a = __ldcs(ps), b = __ldcs(ps + 1);
-            p[0] = a.x; p[1] = a.y; p[2] = a.z; p[3] = a.w;
-            p[4] = b.x; p[5] = b.y; p[6] = b.z; p[7] = b.w;
-            Grad<GT>::load8(D.g, e0, g);
-            CI::load8(D, e0, qm, qv);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                p[j] = 0.0f; g[j] = 0.0f; qm[j] = 0; qv[j] = 0;
-                if (j < cnt) {
-                    p[j] = D.p[e0 + j];
-                    g[j] = Grad<GT>::load1(D.g, e0 + j);
-                    CI::load1(D, e0 + j, qm[j], qv[j]);
-                }
-            }
-        }
-        float sm = 0.0f, sv = 0.0f, vmn = 0.0f;
-        if (cnt > 0) { sm = D.sm[blk]; sv = D.sv[blk]; vmn = D.vmin[blk]; }
-
-        // Dequantise (CUDA/stquant_kernel.cu:163-169).
-        float m[8], v[8];
-        const int tbl_base = use_tbl ? (((tid * kPerThread) >> lb) << kTB) : 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            m[j] = __fmul_rn((float)qm[j], sm);
-            v[j] = use_tbl ? s_tbl[tbl_base + (int)qv[j]] : dequant_v((float)qv[j], sv, vmn);
-        }
-        if (PROF && tid == 0) { const auto t1 = prof_now(); pc[0] += t1 - t0; t0 = t1; }
-
-        // AdamW moments (CUDA/stquant_kernel.cu:174-177).
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            m[j] = adam_m(m[j], g[j], C);
-            v[j] = adam_v(v[j], g[j], C);
-        }
-        if (PROF && tid == 0) { const auto t1 = prof_now(); pc[1] += t1 - t0; t0 = t1; }
-
-        // Parameter update from the unquantised moments (CUDA/stquant_kernel.cu:220-229).
-#pragma unroll
-        for (int j = 0; j < 8; ++j) p[j] = update_p<EXACT_P>(p[j], m[j], v[j], C);
-        if (cnt == kPerThread && D.vec) {
-            float4* pd = reinterpret_cast<float4*>(D.p + e0);
-            __stcs(pd, make_float4(p[0], p[1], p[2], p[3]));
-            __stcs(pd + 1, make_float4(p[4], p[5], p[6], p[7]));
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j < cnt) D.p[e0 + j] = p[j];
-        }
-        if (PROF && tid == 0) { const auto t1 = prof_now(); pc[4] += t1 - t0; t0 = t1; }
-
-        // Block statistics.  NaN seeds make fmaxf/fminf ignore nothing but
-        // NaNs, exactly as the reference's tree over fmaxf/fminf does; missing
-        // tail elements enter as 0 (CUDA/stquant_kernel.cu:92-97).
-        float lv[8];
-        float amax = __int_as_float(0x7fffffff), lmax = amax, lmin = amax;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            lv[j] = log_v_of(v[j]);
-            const bool ok = j < cnt;
-            amax = fmaxf(amax, ok ? fabsf(m[j]) : 0.0f);
-            lmax = fmaxf(lmax, ok ? lv[j] : 0.0f);
-            lmin = fminf(lmin, ok ? lv[j] : 0.0f);
-        }
-        const int gthreads = (1 << lb) >> 3;  // threads per quantisation block
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            if (o < gthreads) {
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-                lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
-            }
-        }
-        if (gthreads > 32) {  // CTA-uniform
-            const int w = tid >> 5;
-            if (lane == 0) { s_red[0][w] = amax; s_red[1][w] = lmax; s_red[2][w] = lmin; }
-            __syncthreads();
-            const int wpg = gthreads >> 5;
-            const int w0 = (w / wpg) * wpg;
-            amax = s_red[0][w0]; lmax = s_red[1][w0]; lmin = s_red[2][w0];
-            for (int k = 1; k < wpg; ++k) {
-                amax = fmaxf(amax, s_red[0][w0 + k]);
-                lmax = fmaxf(lmax, s_red[1][w0 + k]);
-                lmin = fminf(lmin, s_red[2][w0 + k]);
-            }
-        }
-        const float new_sm = scale_m_of(amax, C);
-        const float new_sv = scale_v_of(lmax, lmin, C);
-        if ((tid & (gthreads - 1)) == 0 && blk < nblk) {
-            D.sm[blk] = new_sm;
-            D.sv[blk] = new_sv;
-            D.vmin[blk] = lmin;
-        }
-        if (PROF && tid == 0) { const auto t1 = prof_now(); pc[2] += t1 - t0; t0 = t1; }
-
-        // Requantise (CUDA/stquant_kernel.cu:204-216).
-        const float dm = __fadd_rn(new_sm, 1e-12f), dv = __fadd_rn(new_sv, 1e-12f);
-        const float rdm = __frcp_rn(dm), rdv = __frcp_rn(dv);
-        int mi[8], vi[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float xm = m[j];
-            const float xv = __fsub_rn(lv[j], lmin);
-            bool ok_m = false, ok_v = false;
-            float rm = 0.0f, rv = 0.0f;
-            if (!kAllDouble) {
-                rm = round_ratio_fast(xm, rdm, ok_m);
-                rv = round_ratio_fast(xv, rdv, ok_v);
-            }
-            if (ok_m) {
-                rm = fminf(fmaxf(rm, -C.lm_f), __fsub_rn(C.lm_f, 1.0f));
-                mi[j] = (int)rm;
-            } else {
-                mi[j] = CI::m_int(requant_m_ref(xm, dm, C.lm_d));
-            }
-            if (ok_v) {
-                rv = fminf(fmaxf(rv, 0.0f), C.lv_f);
-                vi[j] = (int)rv;
-            } else {
-                vi[j] = CI::v_int(requant_v_ref(xv, dv, C.lv_d));
-            }
-        }
-        if (cnt == kPerThread && D.vec) {
-            CI::store8(D, e0, mi, vi);
-        } else {
-            // One thread owns all 8 elements, so M8V4 nibble pairs never race.
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j < cnt) CI::store1(D, e0 + j, mi[j], vi[j]);
-        }
-        if (PROF && tid == 0) { const auto t1 = prof_now(); pc[3] += t1 - t0; }
+        float (*red)[kWarps] = s_red[tile & 1];
+        if (s_ctx.vec && tile_e0 + kTile <= n)
+            tile_body<LAYOUT, GT, EXACT_P, PROF, true>(s_ctx, tile_e0, tbl, red, pc, t0);
+        else
+            tile_body<LAYOUT, GT, EXACT_P, PROF, false>(s_ctx, tile_e0, tbl, red, pc, t0);
     }
     if (PROF && tid == 0 && P.prof != nullptr) {
         for (int k = 0; k < kProfSlots; ++k) atomicAdd(P.prof + k, pc[k]);
@@ -491,25 +383,21 @@ __global__ void mdq_step_tree(const LaunchDesc D, unsigned long long* prof) {
     const bool ok = i < D.n;
     unsigned long long t0 = 0;
     unsigned long long pc[kProfSlots] = {0, 0, 0, 0, 0};
-    if (prof && tid == 0) t0 = prof_now();
+    if (prof && tid == 0) t0 = clock64();
 
     const StepConsts C = make_step_consts(D.b1, D.b2, D.lr, D.wd, D.eps, D.step, D.m_bits, D.v_bits);
-    const float sm = D.sm[blk], sv = D.sv[blk], vmn = D.vmin[blk];
+    const float sm = D.t.sm[blk], sv = D.t.sv[blk], vmn = D.t.vmin[blk];
     float g = 0.0f, m = 0.0f, v = 0.0f;
-    int qm = 0;
-    unsigned qv = 0;
+    int qm = 0, qv = 0;
     if (ok) {
-        g = Grad<GT>::load1(D.g, i);
-        CI::load1(D, i, qm, qv);
-        m = __fmul_rn((float)qm, sm);
-        v = dequant_v((float)qv, sv, vmn);
-    }
-    if (prof && tid == 0) { const auto t1 = prof_now(); pc[0] += t1 - t0; t0 = t1; }
-    if (ok) {
+        g = Grad<GT>::load1(D.t.g, i);
+        CI::load1(D.t, i, qm, qv);
+        m = __fmul_rn(CI::kMagicCodes ? small_int_to_float(qm) : (float)qm, sm);
+        v = dequant_v(CI::kMagicCodes ? small_int_to_float(qv) : (float)(unsigned)qv, sv, vmn);
         m = adam_m(m, g, C);
         v = adam_v(v, g, C);
     }
-    if (prof && tid == 0) { const auto t1 = prof_now(); pc[1] += t1 - t0; t0 = t1; }
+    if (prof && tid == 0) prof_mark(pc, 0, t0);
 
     const float lv = ok ? log_v_of(v) : 0.0f;
     float* r0 = s_tree;
@@ -532,40 +420,37 @@ __global__ void mdq_step_tree(const LaunchDesc D, unsigned long long* prof) {
     const float new_vmin = r2[0];
     __syncthreads();  // every thread has read the folded values
     if (tid == 0) {
-        D.sm[blk] = new_sm;
-        D.sv[blk] = new_sv;
-        D.vmin[blk] = new_vmin;
+        D.t.sm[blk] = new_sm;
+        D.t.sv[blk] = new_sv;
+        D.t.vmin[blk] = new_vmin;
     }
-    if (prof && tid == 0) { const auto t1 = prof_now(); pc[2] += t1 - t0; t0 = t1; }
+    if (prof && tid == 0) prof_mark(pc, 2, t0);
 
-    int code_m = 0, code_v = 0;
+    int mw = 0, vw = 0;
     if (ok) {
         const float dm = __fadd_rn(new_sm, 1e-12f), dv = __fadd_rn(new_sv, 1e-12f);
-        const int mi = CI::m_int(requant_m_ref(m, dm, C.lm_d));
-        const int vi = CI::v_int(requant_v_ref(__fsub_rn(lv, new_vmin), dv, C.lv_d));
-        if (LAYOUT != MDQ_LAYOUT_M8V4) CI::store1(D, i, mi, vi);
-        code_m = mi;
-        code_v = vi;
+        mw = CI::m_word(requant_m_ref(m, dm, C.lm_d));
+        vw = CI::v_word(requant_v_ref(__fsub_rn(lv, new_vmin), dv, C.lv_d));
+        if (LAYOUT != MDQ_LAYOUT_M8V4) CI::store1(D.t, i, mw, vw);
     }
     if (LAYOUT == MDQ_LAYOUT_M8V4) {
         // Neighbouring elements share a byte (the block is even, so both lie
         // in this CTA): even elements write first, odd ones after a barrier.
         for (int par = 0; par < 2; ++par) {
-            if (ok && (i & 1) == par) CI::store1(D, i, code_m, code_v);
+            if (ok && (i & 1) == par) CI::store1(D.t, i, mw, vw);
             __syncthreads();
         }
     }
-    if (prof && tid == 0) { const auto t1 = prof_now(); pc[3] += t1 - t0; t0 = t1; }
-    if (ok) {
-        D.p[i] = update_p<EXACT_P>(D.p[i], m, v, C);
-    }
+    if (prof && tid == 0) prof_mark(pc, 3, t0);
+    if (ok) D.t.p[i] = update_p<EXACT_P>(D.t.p[i], m, v, C);
     if (prof && tid == 0) {
-        pc[4] += prof_now() - t0;
+        prof_mark(pc, 4, t0);
         for (int k = 0; k < kProfSlots; ++k) atomicAdd(prof + k, pc[k]);
     }
 }
 
 }  // namespace mdq
+
 
 // ===========================================================================
 // Host side
@@ -660,13 +545,13 @@ mdq_status validate(const mdq_tensor_desc& d, int idx) {
 
 mdq::LaunchDesc to_launch(const mdq_tensor_desc& d) {
     mdq::LaunchDesc L;
-    L.p = d.p;
-    L.g = d.grad;
-    L.m = d.exp_avg;
-    L.v = d.exp_avg_sq;
-    L.sm = d.scale_m;
-    L.sv = d.scale_v;
-    L.vmin = d.v_min;
+    L.t.p = d.p;
+    L.t.g = d.grad;
+    L.t.m = d.exp_avg;
+    L.t.v = d.exp_avg_sq;
+    L.t.sm = d.scale_m;
+    L.t.sv = d.scale_v;
+    L.t.vmin = d.v_min;
     L.n = d.n;
     L.tile_begin = 0;
     L.step = d.step;

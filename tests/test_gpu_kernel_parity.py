@@ -188,3 +188,63 @@ def test_errors_raise(cuda_device):
         prof = torch.zeros(3, dtype=torch.int64, device=cuda_device)
         kernels.fused_mdq_adamw(st.p, g, st.m, st.v, st.sm, st.sv, st.vmin, 0.9, 0.999, 1e-3,
                                 0.01, 1e-8, 1, 8, 256, prof)
+
+
+ADVERSARIAL = ["constant", "zero", "nonfinite", "huge", "tiny", "ramp"]
+
+
+def adversarial_grad(kind, n, step, device):
+    g = torch.Generator().manual_seed(1000 + step)
+    if kind == "constant":      # every element of a block equal: all are extremes
+        x = torch.full((n,), 1e-3 * (1 + step % 3))
+    elif kind == "zero":
+        x = torch.zeros(n)
+    elif kind == "nonfinite":   # NaN / Inf reach codes, scales and p
+        x = torch.randn(n, generator=g) * 1e-3
+        x[::997] = float("nan")
+        x[5::1499] = float("inf")
+        x[7::1777] = -float("inf")
+    elif kind == "huge":
+        x = torch.randn(n, generator=g) * 1e3
+    elif kind == "tiny":
+        x = torch.randn(n, generator=g) * 1e-9
+    else:                       # smooth ramp: many near-equal neighbours
+        x = torch.linspace(-1e-3, 1e-3, n) * (1 + 0.01 * step)
+    return x.to(device)
+
+
+@pytest.mark.parametrize("kind", ADVERSARIAL)
+@pytest.mark.parametrize("layout,bits,block", [("packed4", 4, 128), ("s8u8", 8, 1024),
+                                                ("s8u8", 8, 64), ("s16u16", 16, 256)])
+def test_adversarial_inputs_bit_exact(ref, cuda_device, kind, layout, bits, block):
+    """Degenerate and non-finite gradients: still bit-identical to the reference
+    (NaN compared by bit pattern)."""
+    n = 50_000 + 3
+    a = State(n, block, layout, cuda_device, seed=11)
+    b = a.clone()
+    for s in range(1, 5):
+        g = adversarial_grad(kind, n, s, cuda_device)
+        run_ref(ref, a, g, s, bits)
+        kernels.fused_mdq_adamw(b.p, g, b.m, b.v, b.sm, b.sv, b.vmin, HP["beta1"], HP["beta2"],
+                                HP["lr"], HP["weight_decay"], HP["eps"], s, bits, block)
+        torch.cuda.synchronize()
+        mm = a.mismatches(b)
+        assert all(v == 0 for v in mm.values()), f"{kind} step {s}: {mm}"
+
+
+@pytest.mark.parametrize("layout,bits,block", [("packed4", 4, 128), ("s8u8", 8, 1024),
+                                                ("s8u8", 8, 256), ("packed4", 4, 2048 // 2)])
+def test_long_trajectory_bit_exact(ref, cuda_device, layout, bits, block):
+    """40 steps on 1M elements with bf16 gradients of drifting scale."""
+    n = (1 << 20) + 77
+    a = State(n, block, layout, cuda_device, seed=21)
+    b = a.clone()
+    gen = torch.Generator().manual_seed(5)
+    for s in range(1, 41):
+        g = (torch.randn(n, generator=gen) * 1e-3 * (1 + 0.5 * (s % 7))).bfloat16().to(cuda_device)
+        run_ref(ref, a, g, s, bits)
+        kernels.fused_mdq_adamw(b.p, g, b.m, b.v, b.sm, b.sv, b.vmin, HP["beta1"], HP["beta2"],
+                                HP["lr"], HP["weight_decay"], HP["eps"], s, bits, block)
+    torch.cuda.synchronize()
+    mm = a.mismatches(b)
+    assert all(v == 0 for v in mm.values()), mm
