@@ -1,0 +1,393 @@
+"""Benchmark of the fused quantized-AdamW (MDQ) step on B200.
+
+Workload (its largest point): one flat fp32 parameter
+tensor of 2^30 elements per GPU, p ~ N(0, 0.02^2), bf16 gradients
+~ N(0, 1e-3^2), 4-bit m/v codes in the reference's packed layout, block 2048
+requested (the reference's CUDA path clamps it to a 1024-element quantisation
+block), lr 1e-3, betas (0.9, 0.999), eps 1e-8, weight decay 0.01.  A step is
+one fused step over the whole tensor.  Inputs (~7.3 GB per GPU) exceed the
+126 MB L2, so no flush is needed between steps.
+
+Under torchrun each rank holds its own 2^30-element shard of the optimizer
+state and steps it independently (ZeRO-1 state partitioning; the step itself
+has no data-path collective), so scaling is weak and `value` is the whole
+job's parameters per second: N * 2^30 / (max over ranks of the step time).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "stream-mm2026_b200"))
+sys.path.insert(0, REPO)
+
+METRIC = "fused q-AdamW step Gparams/s & HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+UNIT = "Gparams/s"
+LOG2_N = 30
+BLOCK_REQUESTED = 2048
+BLOCK = min(BLOCK_REQUESTED, 1024)       # CUDA/stquant_opt_simple.py:234
+HP = dict(lr=1e-3, weight_decay=0.01, eps=1e-8, beta1=0.9, beta2=0.999)
+# Algorithmic bytes per element: p read+write 8, bf16 grad 2, packed4 code
+# read+write 2, and three fp32 scales read+written per block.
+BYTES_PER_ELEM = 8 + 2 + 2 + 3 * 4 * 2 / BLOCK
+SPEC_HBM_GBS = 8000.0
+
+
+def config(n_gpus: int) -> dict:
+    return {"workload": "flat fp32 tensor 2^30 elts/GPU, packed 4-bit m/v, bf16 grads, "
+                        "block 2048 (quantised per 1024 as the reference)",
+            "elements_per_gpu": 1 << LOG2_N, "bits": 4, "block_requested": BLOCK_REQUESTED,
+            "quant_block": BLOCK, "grad_dtype": "bf16", "param_dtype": "fp32",
+            "parallelism": f"zero1-state-shard x{n_gpus}" if n_gpus > 1 else "single",
+            "l2": "inputs larger than L2 (7.3 GB/GPU), no flush"}
+
+
+def measured_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}",
+                                      f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=5).stdout.strip()
+                self.samples.append([x.strip() for x in out.split(",")])
+            except (OSError, subprocess.SubprocessError):
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            try:
+                sm.append(float(s[0]))
+                mx = float(s[1])
+                for name, val in zip(names, s[3:7]):
+                    if val.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+def make_state(n, device, seed):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    p = torch.randn(n, device=device, generator=g) * 0.02
+    grad = (torch.randn(n, device=device, generator=g) * 1e-3).to(torch.bfloat16)
+    nb = (n + BLOCK - 1) // BLOCK
+    codes = torch.full((n,), 8, dtype=torch.uint8, device=device)
+    sm = torch.zeros(nb, device=device)
+    sv = torch.zeros(nb, device=device)
+    vmin = torch.full((nb,), -20.0, device=device)
+    return p, grad, codes, sm, sv, vmin
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from mdq_b200 import kernels
+    from mdq_b200._lib import TensorDesc
+    from mdq_b200.kernels import LAYOUT_PACKED4, P_FAST, StepItem
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    n = 1 << LOG2_N
+    p, grad, codes, sm, sv, vmin = make_state(n, device, seed=rank)
+    item = StepItem(p=p, grad=grad, exp_avg=codes, exp_avg_sq=None, scale_m=sm, scale_v=sv,
+                    v_min=vmin, step=1, block=BLOCK, m_bits=4, v_bits=4,
+                    layout=LAYOUT_PACKED4, **HP)
+    descs = (TensorDesc * 1)()
+    stream = torch.cuda.current_stream(device)
+
+    def step(t):
+        item.step = t
+        kernels.fill_desc(descs[0], item)
+        kernels.run_descs(descs, 1, device, P_FAST, stream=stream.cuda_stream)
+
+    t = 0
+    for _ in range(args.warmup):
+        t += 1
+        step(t)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            t += 1
+            step(t)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        x = torch.tensor([ms], device=device)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        ms = float(x.item())
+        dist.barrier()
+
+    # Exact-parameter mode, same workload (extra figure, not the headline).
+    def step_exact(tt):
+        item.step = tt
+        kernels.fill_desc(descs[0], item)
+        kernels.run_descs(descs, 1, device, 1, stream=stream.cuda_stream)
+
+    for _ in range(2):
+        t += 1
+        step_exact(t)
+    start.record(stream)
+    for _ in range(args.steps):
+        t += 1
+        step_exact(t)
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms_exact = start.elapsed_time(end) / args.steps
+
+    e2e_sec = run_e2e(args, device, p, grad, codes, sm, sv, vmin, t)
+    if world > 1:
+        x = torch.tensor([e2e_sec], device=device, dtype=torch.float64)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        e2e_sec = float(x.item())
+    e2e = {"value": round(world * n / e2e_sec / 1e9, 3), "unit": UNIT,
+           "h2d_bytes_per_step": n * 2, "d2h_bytes_per_step": n * 4,
+           "ms_per_step": round(e2e_sec * 1e3, 3),
+           "path": "mdq_b200.step_multi; per step the bf16 gradient comes from pinned host "
+                   "memory and the fp32 parameters go back to it, 16 chunks pipelined"}
+    del p, grad, codes, sm, sv, vmin
+    torch.cuda.empty_cache()
+    return ms, ms_exact, clk.summary(), e2e
+
+
+def run_e2e(args, device, p, grad, codes, sm, sv, vmin, t0):
+    """Same step through the public API (mdq_b200.step_multi) with host
+    buffers: every step copies this step's gradient from pinned host memory
+    and reads the updated parameters back, pipelined over chunks of 2^26
+    elements on separate copy streams.  The optimizer state stays resident."""
+    import torch
+
+    from mdq_b200 import kernels
+    from mdq_b200.kernels import LAYOUT_PACKED4, P_FAST, StepItem
+
+    n = p.numel()
+    chunk = 1 << 26
+    nchunks = n // chunk
+    h_grad = torch.empty(n, dtype=torch.bfloat16, pin_memory=True)
+    h_grad.copy_(grad)
+    h_p = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    h2d, comp, d2h = (torch.cuda.Stream(device) for _ in range(3))
+    cpb = chunk // BLOCK
+    items = []
+    for c in range(nchunks):
+        sl = slice(c * chunk, (c + 1) * chunk)
+        bs = slice(c * cpb, (c + 1) * cpb)
+        items.append(StepItem(p=p[sl], grad=grad[sl], exp_avg=codes[sl], exp_avg_sq=None,
+                              scale_m=sm[bs], scale_v=sv[bs], v_min=vmin[bs], step=1, block=BLOCK,
+                              m_bits=4, v_bits=4, layout=LAYOUT_PACKED4, **HP))
+
+    def one_step(t):
+        done_h2d = []
+        for c in range(nchunks):
+            sl = slice(c * chunk, (c + 1) * chunk)
+            with torch.cuda.stream(h2d):
+                grad[sl].copy_(h_grad[sl], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(h2d)
+                done_h2d.append(e)
+        for c in range(nchunks):
+            sl = slice(c * chunk, (c + 1) * chunk)
+            with torch.cuda.stream(comp):
+                comp.wait_event(done_h2d[c])
+                items[c].step = t
+                kernels.step_multi([items[c]], p_mode=P_FAST)
+                e = torch.cuda.Event()
+                e.record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(e)
+                h_p[sl].copy_(p[sl], non_blocking=True)
+
+    t = t0
+    for _ in range(max(1, args.warmup // 2)):
+        t += 1
+        one_step(t)
+    torch.cuda.synchronize()
+    steps = max(2, min(args.steps, 10))
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        t += 1
+        one_step(t)
+    torch.cuda.synchronize()
+    return (time.perf_counter() - t_start) / steps
+
+
+def traffic_per_launch(n_elems):
+    """DRAM bytes per launch from the committed ncu summary of this kernel,
+    scaled from its capture size to this launch (traffic is proportional)."""
+    path = os.path.join(REPO, "profiles", "mdq_step_tiles_packed4_bf16_b1024.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        per_elem = (d["dram_bytes_read"] + d["dram_bytes_write"]) / d["elements"]
+        return round(per_elem * n_elems), d.get("capture", "")
+    except (OSError, KeyError, ValueError, ZeroDivisionError):
+        return None, None
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the oracle port of the reference kernel on host cores
+# ----------------------------------------------------------------------------
+def cpu_baseline(budget_s=12.0, threads=None):
+    import numpy as np
+
+    from oracle import oracle
+
+    oracle.build()
+    threads = threads or oracle.max_threads()
+    n = 1 << 22                       # config 1: one 2048 x 2048 tensor
+    rng = np.random.default_rng(0)
+    p = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    g = (rng.standard_normal(n) * 1e-3).astype(np.float32)
+    codes = np.full(n, 8, np.uint8)
+    nb = n // BLOCK
+    sm = np.zeros(nb, np.float32)
+    sv = np.zeros(nb, np.float32)
+    vmin = np.full(nb, -20.0, np.float32)
+    steps, t = 0, 0.0
+    t0 = time.perf_counter()
+    while True:
+        steps += 1
+        oracle.step(p, g, oracle.LAYOUT_PACKED4, codes, None, sm, sv, vmin, BLOCK, HP["beta1"],
+                    HP["beta2"], HP["lr"], HP["weight_decay"], HP["eps"], steps, 4, 4,
+                    threads=threads)
+        t = time.perf_counter() - t0
+        if (t >= budget_s and steps >= 3) or steps >= 2000:
+            break
+    return {"value": round(n * steps / t / 1e9, 4), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"{steps} steps x 2^22 elements (oracle/mdq_oracle.c, packed 4-bit, "
+                      f"block {BLOCK}, fp32 grads) in {t:.1f} s"}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    # Each step is one bounded sample: the oracle port over 2^22 elements.
+    base = cpu_baseline(budget_s=max(3.0, min(60.0, 0.5 * (args.steps + args.warmup))))
+    line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round((1 << 22) / (base["value"] * 1e9) * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": config(world), "impl": "reference",
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mdq_b200", choices=["mdq_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    ms, ms_exact, clocks, e2e = run_ours(args, rank, world, local_rank)
+    n = 1 << LOG2_N
+    value = world * n / (ms * 1e-3) / 1e9
+    bytes_launch = n * BYTES_PER_ELEM
+    achieved = bytes_launch / (ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    traffic, capture = traffic_per_launch(n)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": config(world),
+            "hbm_gbs_per_gpu": round(achieved, 1),
+            "pct_of_8tbs": round(100 * achieved / SPEC_HBM_GBS, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "traffic_source": capture,
+                         "algorithmic_bytes_per_launch": round(bytes_launch)},
+            "exact_p_mode": {"value": round(world * n / (ms_exact * 1e-3) / 1e9, 2),
+                             "ms_per_step": round(ms_exact, 4)},
+            "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -46,7 +46,6 @@ template <int LAYOUT> struct Codes;
 // One byte per element: low nibble q_m + 8, high nibble q_v
 // (CUDA/stquant_kernel.cu:52,71-73,130).
 template <> struct Codes<MDQ_LAYOUT_PACKED4> {
-    static constexpr int kTblBits = 4;      // v codes tabulated per block
     static constexpr bool kApproxLog = true;
     static constexpr bool kMagicCodes = true;
     __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
@@ -159,21 +158,17 @@ template <typename MT, typename VT, bool MAGIC> struct CodesPlain {
 };
 
 template <> struct Codes<MDQ_LAYOUT_S8U8> : CodesPlain<int8_t, uint8_t, true> {
-    static constexpr int kTblBits = 0;  // 256 codes per block: decoded per element
     static constexpr bool kApproxLog = true;
 };
 template <> struct Codes<MDQ_LAYOUT_S16U16> : CodesPlain<int16_t, uint16_t, true> {
-    static constexpr int kTblBits = 0;
     static constexpr bool kApproxLog = false;
 };
 template <> struct Codes<MDQ_LAYOUT_S32U32> : CodesPlain<int32_t, uint32_t, false> {
-    static constexpr int kTblBits = 0;
     static constexpr bool kApproxLog = false;
 };
 
 // int8 m codes + v nibbles packed two per byte (element 2i in the low nibble).
 template <> struct Codes<MDQ_LAYOUT_M8V4> {
-    static constexpr int kTblBits = 4;
     static constexpr bool kApproxLog = true;
     static constexpr bool kMagicCodes = true;
     __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {

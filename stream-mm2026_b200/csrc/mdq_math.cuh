@@ -75,11 +75,12 @@ __device__ __forceinline__ float update_p(float w, float m, float v, const StepC
         return __fmaf_rn(-c.step_size, __fdiv_rn(m, denom), w);
     } else {
         // Hardware square root and reciprocal: a few ulp on the update term.
-        float s;
-        asm("sqrt.approx.f32 %0, %1;" : "=f"(s) : "f"(v));
+        float s, r;
+        asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(s) : "f"(v));
         const float denom = __fmaf_rn(s, c.inv_sqrt_bc2, c.eps);
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(denom));
         if (c.wd != 0.0f) w = w * c.decay;
-        return __fmaf_rn(-c.step_size, __fdividef(m, denom), w);
+        return __fmaf_rn(-c.step_size, m * r, w);
     }
 }
 
@@ -128,22 +129,44 @@ __device__ __noinline__ double requant_v_ref(float x, float d, double lv) {
 }
 
 // ---------------------------------------------------------------------------
-// Rounding without conversion instructions.  For |y| <= 2^22, y + 1.5*2^23
-// rounds y to the nearest integer (ties to even) and its bit pattern is
-// 0x4B400000 + rint(y).  `round_word` clamps y to [lo, hi] first (integer
-// bounds; clamping commutes with rounding since rounding is monotone), returns
-// that bit pattern, and sets `ok` when the rounded value provably equals the
-// reference's double-precision round-half-away of the exact quotient: the
-// distance of y to the nearest half-integer must exceed |y| * 2^-21 (the
-// relative error of y = x * RN(1/d)) plus `slack` (any further absolute error
-// of y).  Exact ties never pass, so ties-to-even never decides a code.
+// Rounding.  The reference computes q = round((double)x / (double)d) with
+// round-half-away-from-zero (CUDA/stquant_kernel.cu:205,212), x and d floats.
+// For |x/d| < 2^17 the double quotient never lands on or crosses a
+// half-integer the exact quotient does not (a quotient of floats that is not
+// itself a half-integer stays >= 2^-26 from every half-integer, and the
+// double rounding error is below 2^-36), so q is the integer nearest the
+// exact x/d, with ties away from zero.
+//
+// Here r = rint(y) for an estimate y of x/d, computed without conversion
+// instructions: for |y| <= 2^22, s = y + 1.5*2^23 rounds y to an integer r
+// and has the bit pattern 0x4B400000 + r ("magic word").  r is then checked
+// exactly: |x - r*d| < d/2 holds iff r is the nearest integer to x/d and x/d
+// is not a tie; fma computes x - r*d with one rounding, which preserves a
+// strict comparison with d/2 (a power-of-two multiple of d, exactly
+// representable).  `round_checked` returns the magic word and |x - r*d|;
+// with CORRECT it first moves r one step toward x/d when the remainder shows
+// that y rounded to a neighbour (needed for 16-bit codes, where the estimate
+// y = x * RN(1/d) can be off by more than the distance to a half-integer).
+// A NaN operand gives a NaN remainder, which fails every comparison.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int round_word(float y, float lo, float hi, float slack, bool& ok) {
-    const float yc = fminf(fmaxf(y, lo), hi);  // NaN y -> lo; caught below
-    const float s = __fadd_rn(yc, 12582912.0f);
-    const float r = __fsub_rn(s, 12582912.0f);
-    const float t = fabsf(__fsub_rn(yc, r));
-    ok = __fadd_rn(__fmaf_rn(fabsf(yc), 0x1p-21f, t), slack) < 0.5f && !isnan(y);
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+template <bool CORRECT>
+__device__ __forceinline__ int round_checked(float y, float x, float d, float half_d, float& rem) {
+    float s = __fadd_rn(y, 12582912.0f);
+    float r = __fsub_rn(s, 12582912.0f);
+    float e = __fmaf_rn(-r, d, x);
+    if (CORRECT) {
+        const float stp = e >= half_d ? 1.0f : (e <= -half_d ? -1.0f : 0.0f);
+        s = __fadd_rn(s, stp);
+        r = __fadd_rn(r, stp);
+        e = __fmaf_rn(-r, d, x);
+    }
+    rem = fabsf(e);
     return __float_as_int(s);
 }
 

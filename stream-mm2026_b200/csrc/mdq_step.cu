@@ -4,18 +4,20 @@
 // -------------
 // The reference runs one thread per element and one CTA per quantisation block
 // (CUDA/stquant_kernel.cu:61,421-422) with three shared-memory tree reductions
-// per CTA.  Here a persistent grid of 256-thread CTAs walks "tiles" of 2048
+// per CTA and a double-precision divide per code.  Here a persistent grid of
+// 256-thread CTAs (3 per SM) walks contiguous ranges of "tiles" of 2048
 // consecutive elements of one tensor; each thread owns 8 consecutive elements,
-// loaded and stored with 128-bit (p, g) and 32/64/128-bit (codes) accesses.  A
-// quantisation block of B elements (power of two, 8..2048) is owned by B/8
-// consecutive threads, so the block max/min reductions are warp shuffles (and,
-// for B > 256, one shared-memory exchange).  For 4-bit v codes (and 8-bit v
-// codes with B >= 512) the 2^k possible dequantised v values of each block are
-// tabulated once in shared memory, replacing one expf per element by a shared
-// load of the identical value.  Tiles of all tensors of one layout / gradient
-// dtype are scheduled in one launch from a descriptor table passed as a
-// __grid_constant__ kernel parameter, so nothing is allocated and nothing is
-// copied host-to-device per step.
+// loaded and stored with 128-bit (p, g) and 32/64/128-bit (codes) streaming
+// accesses.  A quantisation block of B elements (power of two, 8..2048) is
+// owned by B/8 consecutive threads, so its max/min reductions are xor
+// shuffles or one redux.sync (and, for B > 256, one shared-memory exchange).
+// The block's log extremes come from one logf of the extreme v (logf is
+// monotone), codes from a float estimate whose exactness is checked by an fma
+// remainder, with the reference's double expression as the rare fallback.
+// Tiles of all tensors of one layout / gradient dtype are scheduled in one
+// launch from a descriptor table passed as a __grid_constant__ kernel
+// parameter, so nothing is allocated and nothing is copied host-to-device per
+// step.
 //
 // Block sizes that are not a power of two, or below 8, take a second kernel
 // that keeps the reference's one-thread-per-element shape and reproduces its
@@ -86,18 +88,32 @@ __device__ int find_desc(const LaunchParams<CAP>& P, int tile) {
 }
 
 // Max (bit k of MAXMASK set) or min of NV values over the `gthreads`
-// consecutive threads that own one quantisation block: xor shuffles inside a
-// warp, then one shared-memory exchange when a block spans several warps
-// (gthreads is uniform over the CTA, so the barrier is too).
+// consecutive threads that own one quantisation block (gthreads is uniform
+// over the CTA, so the branches and the barrier are too).  Inside a warp:
+// redux.sync when the block covers whole warps, xor shuffles otherwise; then
+// one shared-memory exchange when a block spans several warps.  Every step is
+// an fmaxf / fminf, which skip NaNs as the reference's reduction does.
 template <unsigned MAXMASK, int NV>
 __device__ __forceinline__ void group_reduce(float (&x)[NV], int gthreads, float (*red)[kWarps]) {
+    if (gthreads >= 32) {
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        if (o < gthreads) {
+        for (int k = 0; k < NV; ++k) {
+            float r;
+            if ((MAXMASK >> k) & 1u)
+                asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x[k]));
+            else
+                asm volatile("redux.sync.min.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x[k]));
+            x[k] = r;
+        }
+    } else {
 #pragma unroll
-            for (int k = 0; k < NV; ++k) {
-                const float y = __shfl_xor_sync(0xffffffffu, x[k], o);
-                x[k] = ((MAXMASK >> k) & 1u) ? fmaxf(x[k], y) : fminf(x[k], y);
+        for (int o = 1; o < 32; o <<= 1) {
+            if (o < gthreads) {
+#pragma unroll
+                for (int k = 0; k < NV; ++k) {
+                    const float y = __shfl_xor_sync(0xffffffffu, x[k], o);
+                    x[k] = ((MAXMASK >> k) & 1u) ? fmaxf(x[k], y) : fminf(x[k], y);
+                }
             }
         }
     }
@@ -129,10 +145,9 @@ __device__ __forceinline__ void prof_mark(unsigned long long (&pc)[kProfSlots], 
 
 // One tile of 2048 elements.  FULL: every thread owns 8 in-range elements and
 // all pointers allow vector access; otherwise element-wise guarded access.
-// `tbl` is this warp's dequantised-v table (nullptr when not tabulated) and
-// `red` this tile's reduction scratch.
+// `red` is this tile's reduction scratch.
 template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL>
-__device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0, const float* tbl,
+__device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                                           float (*red)[kWarps],
                                           unsigned long long (&pc)[kProfSlots],
                                           unsigned long long& t0) {
@@ -179,20 +194,13 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0, con
 
     // ---- dequantise, AdamW moments, parameter update -------------------
     // (CUDA/stquant_kernel.cu:163-177, 220-229)
-    // Table row of this thread's block: blocks of <= 256 elements lie inside
-    // one warp's 256 elements, larger ones cover the whole warp.
-    const int trow = lb <= 8 ? ((((tid & 31) * kPerThread) >> lb) << 4) : 0;
     float m[8], v[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const float qmf = kMagicC ? small_int_to_float(qm[j]) : (float)qm[j];
         m[j] = __fmul_rn(qmf, sm);
-        if (CI::kTblBits > 0 && tbl != nullptr) {
-            v[j] = tbl[trow + qv[j]];
-        } else {
-            const float qvf = kMagicC ? small_int_to_float(qv[j]) : (float)(unsigned)qv[j];
-            v[j] = dequant_v(qvf, sv, vmn);
-        }
+        const float qvf = kMagicC ? small_int_to_float(qv[j]) : (float)(unsigned)qv[j];
+        v[j] = dequant_v(qvf, sv, vmn);
     }
     if (PROF && tid == 0) prof_mark(pc, 0, t0);
 #pragma unroll
@@ -221,15 +229,15 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0, con
     // x = 1 (log v = 0, :92-93).
     float x[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) x[j] = __fadd_rn(v[j], 1e-12f);
+    for (int j = 0; j < 8; ++j) x[j] = (FULL || j < cnt) ? __fadd_rn(v[j], 1e-12f) : 1.0f;
     const int gthreads = (1 << lb) >> 3;
     float st[3] = {kNaN, kNaN, kNaN};
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const bool ok = FULL || j < cnt;
         st[0] = fmaxf(st[0], ok ? fabsf(m[j]) : 0.0f);
-        st[1] = fmaxf(st[1], ok ? x[j] : 1.0f);
-        st[2] = fminf(st[2], ok ? x[j] : 1.0f);
+        st[1] = fmaxf(st[1], x[j]);
+        st[2] = fminf(st[2], x[j]);
     }
     group_reduce<0b011u>(st, gthreads, red);
     const float lmax = logf(st[1]);
@@ -246,35 +254,47 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0, con
     // ---- requantise (CUDA/stquant_kernel.cu:204-216) --------------------
     const float dm = __fadd_rn(new_sm, 1e-12f), dv = __fadd_rn(new_sv, 1e-12f);
     const float rdm = __frcp_rn(dm), rdv = __frcp_rn(dv);
-    // Bound on |(a - lmin) - RN(logf(x) - lmin)|: the approximation error plus
-    // one ulp of a difference below 128 (logs of floats >= 1e-12 lie in
-    // [-27.7, 88.8]), scaled to code units.
-    float slack_v = 0.0f;
-    if (kApprox)
-        slack_v = __fmul_rn(__fadd_rn(log_tol(fmaxf(fabsf(lmax), fabsf(lmin))), 0x1p-17f),
-                            __fmul_rn(rdv, 1.001f));
-    const float mlo = -C.lm_f, mhi = __fsub_rn(C.lm_f, 1.0f), vhi = C.lv_f;
+    const float half_dm = 0.5f * dm, half_dv = 0.5f * dv;
+    // v codes from the approximate log see X' = RN(a - lmin) instead of the
+    // reference's X = RN(logf(x) - lmin): |X' - X| <= log_tol + one ulp of a
+    // difference of at most max(lmax - lmin, 1) (logs of floats >= 1e-12 lie
+    // in [-27.7, 88.8]).  The remainder test absorbs that error.
+    float thr_v = half_dv;
+    if (kApprox) {
+        const float errx = __fmaf_rn(fmaxf(__fsub_rn(lmax, lmin), 1.0f), 0x1p-22f,
+                                     log_tol(fmaxf(fabsf(lmax), fabsf(lmin))));
+        // (less one relative 2^-22 of d/2 for the rounding of the remainder)
+        thr_v = __fmaf_rn(-errx, 1.001f, __fmul_rn(half_dv, 1.0f - 0x1p-22f));
+    }
+    // 16-bit codes can be mis-rounded by the reciprocal estimate; correct them.
+    constexpr bool kCorrect = !kApprox;
+    // The positive m extreme rounds to L and clamps to L - 1; every other
+    // accepted code already lies in its level range (|m| <= max|m| bounds
+    // m / dm by L (1 + 2^-22); accepted v codes have |X'/dv - r| < 1/2 with
+    // X' in [-errx, lmax - lmin + errx]).
+    const int mw_hi = kMagicBits + (int)C.lm_f - 1;
     int mw[8], vw[8];
-    unsigned redo = 0;
+    float rem_m = 0.0f, rem_v = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        bool okm = false, okv = false;
-        mw[j] = 0;
-        vw[j] = 0;
-        if (kMagicC) {
-            const float lj = kApprox ? approx_ln(x[j]) : logf(x[j]);
-            mw[j] = round_word(__fmul_rn(m[j], rdm), mlo, mhi, 0.0f, okm);
-            vw[j] = round_word(__fmul_rn(__fsub_rn(lj, lmin), rdv), 0.0f, vhi, slack_v, okv);
-        }
-        redo |= (okm ? 0u : 1u) << (2 * j);
-        redo |= (okv ? 0u : 2u) << (2 * j);
+        float r;
+        mw[j] = min(round_checked<kCorrect>(__fmul_rn(m[j], rdm), m[j], dm, half_dm, r), mw_hi);
+        rem_m = max_nan(rem_m, r);
+        const float xv = __fsub_rn(kApprox ? approx_ln(x[j]) : logf(x[j]), lmin);
+        vw[j] = round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
+        rem_v = max_nan(rem_v, r);
     }
-    if (redo != 0) {
-        // The reference's double-precision expression for undecided codes.
+    if (!kMagicC || !(rem_m < half_dm && rem_v < thr_v)) {
+        // Rare: codes that fail their check take the reference's
+        // double-precision expression (all of them for 32-bit codes).
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            if ((redo >> (2 * j)) & 1u) mw[j] = CI::m_word(requant_m_ref(m[j], dm, C.lm_d));
-            if ((redo >> (2 * j)) & 2u)
+            float r;
+            round_checked<kCorrect>(__fmul_rn(m[j], rdm), m[j], dm, half_dm, r);
+            if (!kMagicC || !(r < half_dm)) mw[j] = CI::m_word(requant_m_ref(m[j], dm, C.lm_d));
+            const float xv = __fsub_rn(kApprox ? approx_ln(x[j]) : logf(x[j]), lmin);
+            round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
+            if (!kMagicC || !(r < thr_v))
                 vw[j] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[j]), lmin), dv, C.lv_d));
         }
     }
@@ -295,18 +315,14 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0, con
 // CTA-wide barriers happen only at a tensor switch and, for blocks spanning
 // several warps, inside the block reduction.
 // ---------------------------------------------------------------------------
-constexpr int kTblPerWarp = 128;  // (256 / 32 blocks) x 16 codes at most
-
 template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP>
 __global__ void __launch_bounds__(kThreads, MDQ_MIN_CTAS_PER_SM)
 mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
     using CI = Codes<LAYOUT>;
-    __shared__ float s_tbl[kWarps][kTblPerWarp];
     __shared__ float s_red[2][3][kWarps];  // alternates by tile
     __shared__ TileCtx s_ctx;
 
     const int tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
     unsigned long long pc[kProfSlots] = {0, 0, 0, 0, 0};
     const int64_t total = P.total_tiles;
     const int tile_lo = (int)(total * blockIdx.x / gridDim.x);
@@ -332,34 +348,14 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
         }
         unsigned long long t0 = 0;
         if (PROF && tid == 0) t0 = clock64();
-        const int lb = s_ctx.lb;
         const int64_t n = s_ctx.n;
         const int64_t tile_e0 = (int64_t)(tile - s_ctx.tile_begin) << kLogTile;
 
-        // This warp's dequantised-v table for 4-bit v codes: entry (block,
-        // code) = expf(code * sv + v_min), the value the reference computes
-        // per element (CUDA/stquant_kernel.cu:169).  Blocks of 8 or 16
-        // elements gain nothing from it and decode per element.
-        const float* tbl = nullptr;
-        if (CI::kTblBits == 4 && lb >= 5) {
-            float* row = s_tbl[warp];
-            const int64_t wb0 = (tile_e0 + (warp << 8)) >> lb;  // first block of this warp
-            const int entries = lb <= 8 ? (256 >> lb) << 4 : 16;
-            const int64_t nblk = (n + ((int64_t)1 << lb) - 1) >> lb;
-            __syncwarp();  // lanes are done with the previous tile's entries
-            for (int j = lane; j < entries; j += 32) {
-                const int64_t b = wb0 + (j >> 4);
-                row[j] = b < nblk ? dequant_v((float)(j & 15), s_ctx.t.sv[b], s_ctx.t.vmin[b])
-                                  : 0.0f;
-            }
-            __syncwarp();
-            tbl = row;
-        }
         float (*red)[kWarps] = s_red[tile & 1];
         if (s_ctx.vec && tile_e0 + kTile <= n)
-            tile_body<LAYOUT, GT, EXACT_P, PROF, true>(s_ctx, tile_e0, tbl, red, pc, t0);
+            tile_body<LAYOUT, GT, EXACT_P, PROF, true>(s_ctx, tile_e0, red, pc, t0);
         else
-            tile_body<LAYOUT, GT, EXACT_P, PROF, false>(s_ctx, tile_e0, tbl, red, pc, t0);
+            tile_body<LAYOUT, GT, EXACT_P, PROF, false>(s_ctx, tile_e0, red, pc, t0);
     }
     if (PROF && tid == 0 && P.prof != nullptr) {
         for (int k = 0; k < kProfSlots; ++k) atomicAdd(P.prof + k, pc[k]);
