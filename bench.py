@@ -37,6 +37,7 @@ UNIT = "Gparams/s"
 LOG2_N = 30
 BLOCK_REQUESTED = 2048
 BLOCK = min(BLOCK_REQUESTED, 1024)       # CUDA/stquant_opt_simple.py:234
+# --log2-elements / --block change these for small profiling cases.
 HP = dict(lr=1e-3, weight_decay=0.01, eps=1e-8, beta1=0.9, beta2=0.999)
 # Algorithmic bytes per element: p read+write 8, bf16 grad 2, packed4 code
 # read+write 2, and three fp32 scales read+written per block.
@@ -45,12 +46,12 @@ SPEC_HBM_GBS = 8000.0
 
 
 def config(n_gpus: int) -> dict:
-    return {"workload": "flat fp32 tensor 2^30 elts/GPU, packed 4-bit m/v, bf16 grads, "
-                        "block 2048 (quantised per 1024 as the reference)",
+    return {"workload": f"flat fp32 tensor 2^{LOG2_N} elts/GPU, packed 4-bit m/v, bf16 grads, "
+                        f"block {BLOCK_REQUESTED} (quantised per {BLOCK} as the reference)",
             "elements_per_gpu": 1 << LOG2_N, "bits": 4, "block_requested": BLOCK_REQUESTED,
             "quant_block": BLOCK, "grad_dtype": "bf16", "param_dtype": "fp32",
             "parallelism": f"zero1-state-shard x{n_gpus}" if n_gpus > 1 else "single",
-            "l2": "inputs larger than L2 (7.3 GB/GPU), no flush"}
+            "l2": f"inputs larger than L2 ({(1 << LOG2_N) * 7 / 2**30:.1f} GiB/GPU), no flush"}
 
 
 def measured_peak():
@@ -191,6 +192,8 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ms_exact = start.elapsed_time(end) / args.steps
 
+    if args.no_e2e:
+        return ms, ms_exact, clk.summary(), None
     e2e_sec = run_e2e(args, device, p, grad, codes, sm, sv, vmin, t)
     if world > 1:
         x = torch.tensor([e2e_sec], device=device, dtype=torch.float64)
@@ -270,7 +273,7 @@ def run_e2e(args, device, p, grad, codes, sm, sv, vmin, t0):
 def traffic_per_launch(n_elems):
     """DRAM bytes per launch from the committed ncu summary of this kernel,
     scaled from its capture size to this launch (traffic is proportional)."""
-    path = os.path.join(REPO, "profiles", "mdq_step_tiles_packed4_bf16_b1024.json")
+    path = os.path.join(REPO, "profiles", f"mdq_step_tiles_packed4_bf16_b{BLOCK}.json")
     try:
         with open(path) as f:
             d = json.load(f)
@@ -339,7 +342,16 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mdq_b200", choices=["mdq_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--log2-elements", type=int, default=30,
+                    help="elements per GPU = 2^k (profiling cases use smaller k)")
+    ap.add_argument("--block", type=int, default=2048,
+                    help="requested block; quantised per min(block, 1024) as the reference")
     args = ap.parse_args()
+    global LOG2_N, BLOCK_REQUESTED, BLOCK, BYTES_PER_ELEM
+    LOG2_N, BLOCK_REQUESTED = args.log2_elements, args.block
+    BLOCK = min(BLOCK_REQUESTED, 1024)
+    BYTES_PER_ELEM = 8 + 2 + 2 + 3 * 4 * 2 / BLOCK
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
