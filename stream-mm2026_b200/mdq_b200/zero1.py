@@ -1,0 +1,316 @@
+"""ZeRO-1 optimizer-state sharding for the fused MDQ step.
+
+Replaces the reference's sharding role of DeepSpeed ZeRO-2
+(CUDA/7B/llama7b_common.py:90-97) and the DDP gradient all-reduce before the
+step (baseline/pretrain_gpt.py:235).  Each rank keeps the low-bit moments and
+block scales of 1/world of the parameters only:
+
+  1. gradients live in one flat buffer (``flat_grad``; ``p.grad`` are views),
+     reduce-scattered (average) so each rank receives its shard;
+  2. the fused step updates the rank's shard of the flat fp32 parameters;
+  3. the parameters are all-gathered in place, so every rank's model sees the
+     update (``p.data`` are views of ``flat_param``).
+
+Layout.  Parameter i occupies [off_i, off_i + n_i) of the flat buffers, with
+off_i a multiple of the quantisation block B and the segment padded to a whole
+number of blocks, so a block never spans two parameters and a parameter's last
+(partial) block keeps the reference's tail semantics (CUDA/stquant_kernel.cu:
+92-97).  The flat length is padded to world * S with S a multiple of B; rank r
+owns [r*S, (r+1)*S).  A parameter may span ranks: each rank holds the pieces
+of it that fall in its shard, cut at block boundaries, so the sharded step
+computes exactly the codes, scales and parameters of the unsharded one.
+
+Bit policy.  The reference scores each tensor from torch reductions of its
+full gradient (CUDA/stquant_opt_simple.py:94-98).  No rank holds a full
+gradient here, so each rank sums (sum g, sum g^2, sum |g|, count) over its
+pieces, the sums are all-reduced, and n_l, r_l (unbiased std / mean|g|) and v_l
+follow in float64.  These agree with the reference's float32 statistics to
+rounding, so a score within ~1e-6 of a threshold (24 / 12 / 6.8) can pick the
+other bit width; with ``fixed_bits`` the sharded step is bit-exact.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import kernels
+from ._lib import TensorDesc
+from .optim import MDQAdamWSimpleFusedIO, _zero_codes
+
+
+@dataclass
+class Piece:
+    """Part of parameter `param` on this rank: elements [start, start + n) of
+    the parameter, at `flat_off` in the flat buffers (block-aligned)."""
+
+    param: int
+    start: int
+    n: int
+    flat_off: int
+
+
+class ShardLayout:
+    """Block-aligned placement of parameters in flat buffers and shards."""
+
+    def __init__(self, numels: List[int], block: int, world: int):
+        self.block = block
+        self.world = world
+        self.numels = list(numels)
+        self.offsets = []
+        off = 0
+        for n in numels:
+            self.offsets.append(off)
+            off += -(-n // block) * block
+        blocks = off // block
+        self.shard = -(-blocks // world) * block if blocks else block
+        self.total = self.shard * world
+
+    def pieces(self, rank: int) -> List[Piece]:
+        lo, hi = rank * self.shard, (rank + 1) * self.shard
+        out = []
+        for i, (off, n) in enumerate(zip(self.offsets, self.numels)):
+            a, b = max(off, lo), min(off + n, hi)
+            if a < b:
+                out.append(Piece(param=i, start=a - off, n=b - a, flat_off=a))
+        return out
+
+
+class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
+    """State-sharded MDQ-AdamW (FusedIO semantics per parameter piece).
+
+    Arguments are those of the reference optimizer plus ``process_group``
+    (default: the world group) and ``grad_dtype`` (fp32 or bf16 flat
+    gradients).  The block is one per optimizer (``block_size``, clamped to
+    1024 unless ``exact_block``).
+    """
+
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                 alpha=0.9, layer_count=24, batch_size=32, update_freq=20, block_size=256,
+                 *, process_group=None, grad_dtype=torch.float32, **kw):
+        super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
+                         alpha=alpha, layer_count=layer_count, batch_size=batch_size,
+                         update_freq=update_freq, block_size=block_size, **kw)
+        blocks = {self._block_of(g) for g in self.param_groups}
+        if len(blocks) != 1:
+            raise ValueError("ZeroMDQAdamW needs one block_size for all param groups")
+        self.block = blocks.pop()
+        self.group = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        self.params = [p for g in self.param_groups for p in g["params"]]
+        self.param_group_of = [g for g in self.param_groups for _ in g["params"]]
+        for p in self.params:
+            if p.dtype != torch.float32:
+                raise RuntimeError("MDQ parameters must be float32")
+        dev = self.params[0].device
+        self.layout = ShardLayout([p.numel() for p in self.params], self.block, self.world)
+        self.flat_param = torch.zeros(self.layout.total, dtype=torch.float32, device=dev)
+        self.flat_grad = torch.zeros(self.layout.total, dtype=grad_dtype, device=dev)
+        for p, off in zip(self.params, self.layout.offsets):
+            n = p.numel()
+            self.flat_param[off:off + n].copy_(p.detach().reshape(-1))
+            p.data = self.flat_param[off:off + n].view_as(p)
+            p.grad = self.flat_grad[off:off + n].view_as(p)
+        self.pieces = self.layout.pieces(self.rank)
+        s = self.layout.shard
+        self.param_shard = self.flat_param[self.rank * s:(self.rank + 1) * s]
+        self.grad_shard = self.flat_grad[self.rank * s:(self.rank + 1) * s]
+        self._descs = None
+
+    # ------------------------------------------------------------------
+    def zero_grad(self, set_to_none: bool = False):
+        """Zero the flat gradient buffer (the views stay attached)."""
+        self.flat_grad.zero_()
+
+    def _piece_state(self, pc: Piece):
+        """State of one local piece, initialised as the reference initialises
+        a tensor's state (CUDA/stquant_opt_simple.py:212-225)."""
+        p = self.params[pc.param]
+        st = self.state[p]
+        if len(st) == 0:
+            proxy = self.param_shard[pc.flat_off - self.rank * self.layout.shard:][:pc.n]
+            nb = -(-pc.n // self.block)
+            st["step"] = 0
+            if self.fixed_bits is None:
+                st["exp_avg"] = torch.zeros(pc.n, dtype=torch.int16, device=p.device)
+                st["exp_avg_sq"] = torch.zeros(pc.n, dtype=torch.uint16, device=p.device)
+                st["current_bit"] = 16
+            else:
+                lay = kernels.layout_for_bits(*self.fixed_bits)
+                st["exp_avg"], st["exp_avg_sq"] = _zero_codes(proxy, lay)
+                st["current_bit"] = max(self.fixed_bits)
+            st["scale_m"] = torch.zeros(nb, dtype=torch.float32, device=p.device)
+            st["scale_v"] = torch.zeros(nb, dtype=torch.float32, device=p.device)
+            st["v_min"] = torch.full((nb,), -20.0, dtype=torch.float32, device=p.device)
+            st["last_score"] = torch.tensor(12.0, device=p.device)
+            st["piece"] = (pc.start, pc.n)
+        return st
+
+    def _piece_views(self, pc: Piece):
+        o = pc.flat_off - self.rank * self.layout.shard
+        return self.param_shard[o:o + pc.n], self.grad_shard[o:o + pc.n]
+
+    # ------------------------------------------------------------------
+    def _reduce_scatter_grads(self):
+        if self.world == 1:
+            return
+        if dist.get_backend(self.group) == "nccl":
+            dist.reduce_scatter_tensor(self.grad_shard, self.flat_grad, op=dist.ReduceOp.AVG,
+                                       group=self.group)
+        else:
+            # gloo has no reduce-scatter: all-reduce, then every rank reads its shard.
+            dist.all_reduce(self.flat_grad, group=self.group)
+            self.flat_grad.div_(self.world)
+
+    def _all_gather_params(self):
+        if self.world == 1:
+            return
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(self.flat_param, self.param_shard, group=self.group)
+        else:
+            parts = list(self.flat_param.chunk(self.world))
+            dist.all_gather(parts, self.param_shard.clone(), group=self.group)
+
+    def _global_grad_stats(self):
+        """Per-parameter [n_l, r_l, v_l] from all-reduced partial sums."""
+        sums = torch.zeros(len(self.params), 4, dtype=torch.float64,
+                           device=self.flat_grad.device)
+        for pc in self.pieces:
+            _, g = self._piece_views(pc)
+            g64 = g.double()
+            sums[pc.param, 0] += g64.sum()
+            sums[pc.param, 1] += (g64 * g64).sum()
+            sums[pc.param, 2] += g64.abs().sum()
+            sums[pc.param, 3] += pc.n
+        if self.world > 1:
+            dist.all_reduce(sums, group=self.group)
+        s, s2, sa, cnt = sums.unbind(1)
+        mean_sq = s2 / cnt
+        var = (s2 - s * s / cnt) / (cnt - 1)
+        n_l = torch.sqrt(mean_sq)
+        r_l = torch.sqrt(var.clamp_min(0)) / (sa / cnt + 1e-12)
+        return torch.stack([n_l, r_l, mean_sq], 1).float()
+
+    def _decide_bits_sharded(self):
+        stats = self._global_grad_stats()
+        avg = stats.mean(0)
+        if self.n_ema is None:
+            self.n_ema, self.r_ema, self.v_global_ema = avg[0], avg[1], avg[2]
+        else:
+            a = self.param_groups[0]["alpha"]
+            self.n_ema = a * avg[0] + (1 - a) * self.n_ema
+            self.r_ema = a * avg[1] + (1 - a) * self.r_ema
+            self.v_global_ema = a * avg[2] + (1 - a) * self.v_global_ema
+        tau = self.param_groups[0]["tau"]
+        scores = []
+        for i, p in enumerate(self.params):
+            st = self.state[p]
+            n_l, r_l, v_l = stats[i]
+            s_t = 1.0 + (1.0 / torch.cosh(torch.tensor(st["step"] / tau, device=p.device,
+                                                        dtype=torch.float32)))
+            score = (7.2 + torch.log2(r_l / (self.r_ema + 1e-12))
+                     + torch.log2(n_l / (self.n_ema + 1e-12)) + torch.log2(s_t)
+                     + torch.log2(v_l / (self.v_global_ema + 1e-12)))
+            st["last_score"] = score
+            scores.append(score)
+        for p, s in zip(self.params, torch.stack(scores).cpu().tolist()):
+            self.state[p]["current_bit"] = self._score_to_bits(s)
+
+    # ------------------------------------------------------------------
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        self.total_steps += 1
+        self.last_step_timings = {"quant_dequant_unpack_ms": 0.0, "quant_dequant_pack_ms": 0.0,
+                                  "mdq_fused_io_fast_path_params": 0,
+                                  "mdq_fused_io_fallback_params": 0}
+        self._reduce_scatter_grads()
+        for pc in self.pieces:
+            self._piece_state(pc)
+        # A rank without a piece of some parameter still needs its step counter
+        # and bits, which every rank derives identically.
+        for p in self.params:
+            st = self.state[p]
+            if len(st) == 0:
+                st["step"] = 0
+                st["current_bit"] = 16 if self.fixed_bits is None else max(self.fixed_bits)
+                st["last_score"] = torch.tensor(12.0, device=p.device)
+        uf = self.param_groups[0]["update_freq"]
+        if self.fixed_bits is None and ((self.total_steps % uf == 0) or self.total_steps < 5):
+            self._decide_bits_sharded()
+
+        items, repack = [], []
+        held = {pc.param: pc for pc in self.pieces}
+        for i, p in enumerate(self.params):
+            st = self.state[p]
+            if i not in held:
+                # Same step counting as the holders (FusedIO, incl. the double
+                # increment when the storage would have to change layout).
+                bits = int(st["current_bit"])
+                st["step"] += 1
+                st.setdefault("_layout_bits", 16 if self.fixed_bits is None else bits)
+                if self.fixed_bits is None and st["_layout_bits"] != bits:
+                    st["step"] += 1
+                    st["_layout_bits"] = bits
+                continue
+            pc = held[i]
+            pv, gv = self._piece_views(pc)
+            first = len(items)
+            # The shared FusedIO logic (step counting, storage align / pack)
+            # runs on the piece's state; its step item then points at the
+            # piece's views of the flat buffers.
+            self._prepare_param(p, self.param_group_of[i], items, repack)
+            for it in items[first:]:
+                it.p, it.grad = pv, gv
+            st["_layout_bits"] = int(st["current_bit"])
+        device = self.flat_param.device
+        self._launch(items, device)
+        for st, bits in repack:
+            self._pack_momentum_storage(st, bits)
+        self._all_gather_params()
+        return loss
+
+    # ------------------------------------------------------------------
+    def consolidated_state_dict(self):
+        """The unsharded per-parameter state (reference layout) on every rank:
+        pieces are gathered and concatenated in parameter order."""
+        local = []
+        for pc in self.pieces:
+            st = self.state[self.params[pc.param]]
+            # Transported as numpy: torch's object pickling mishandles uint16/32.
+            local.append((pc.param, pc.start,
+                          {k: (v.detach().cpu().numpy() if torch.is_tensor(v) else v)
+                           for k, v in st.items() if k not in ("piece", "_layout_bits")}))
+        if self.world > 1:
+            everything = [None] * self.world
+            dist.all_gather_object(everything, local, group=self.group)
+        else:
+            everything = [local]
+        by_param = {}
+        for rank_list in everything:
+            for i, start, st in rank_list:
+                st = {k: (torch.from_numpy(v) if hasattr(v, "dtype") and hasattr(v, "shape")
+                          else v) for k, v in st.items()}
+                by_param.setdefault(i, []).append((start, st))
+        state = {}
+        for i, parts in by_param.items():
+            parts.sort(key=lambda t: t[0])
+            first = parts[0][1]
+            full = {k: first[k] for k in ("step", "current_bit", "last_score")}
+            for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
+                ts = [st[k] for _, st in parts if st[k].numel() or k != "exp_avg_sq"]
+                full[k] = torch.cat(ts) if ts else first[k]
+            state[i] = full
+        return {"state": state,
+                "param_groups": [{k: v for k, v in g.items() if k != "params"}
+                                 for g in self.param_groups],
+                "mdq_global_stats": {"n_ema": self.n_ema, "r_ema": self.r_ema,
+                                     "v_global_ema": self.v_global_ema,
+                                     "total_steps": self.total_steps}}
