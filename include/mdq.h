@@ -148,6 +148,22 @@ mdq_status mdq_fused_adamw(float* p, const void* grad, int32_t grad_dtype,
                            int32_t step, int32_t bits, int32_t block_size,
                            unsigned long long* profile_cycles, cudaStream_t stream);
 
+/*
+ * Per-tensor gradient statistics for the bit-width policy in one fused pass:
+ * out[4*i .. 4*i+3] = (sum g, sum g^2, sum |g|, count) in float64 for
+ * grads[i] (counts[i] elements of grad_dtype, MDQ_F32 or MDQ_BF16).  Replaces
+ * the three torch reductions per tensor of _compute_grad_stats
+ * (CUDA/stquant_opt_simple.py:94-98); n_l, r_l and v_l follow from the sums.
+ * `workspace` is caller-owned device memory of at least the size reported by
+ * mdq_grad_stats_workspace_bytes; results are deterministic (fixed summation
+ * order, no atomics).  `out` is device memory and is overwritten.
+ */
+mdq_status mdq_grad_stats_workspace_bytes(const int64_t* counts, int32_t n_tensors,
+                                          int64_t* bytes);
+mdq_status mdq_grad_stats_multi(const void* const* grads, const int64_t* counts,
+                                int32_t n_tensors, int32_t grad_dtype, double* out,
+                                void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+
 /* Message describing the calling thread's most recent failure ("" if none). */
 const char* mdq_last_error(void);
 

@@ -452,15 +452,28 @@ __global__ void mdq_step_tree(const LaunchDesc D, unsigned long long* prof) {
 // Host side
 // ===========================================================================
 namespace {
-
 thread_local char g_err[512] = "";
+}  // namespace
 
-mdq_status fail(mdq_status s, const char* fmt, ...) {
+// The library's per-thread error record, shared by every entry point.
+mdq_status mdq_fail(mdq_status s, const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
     vsnprintf(g_err, sizeof(g_err), fmt, ap);
     va_end(ap);
     return s;
+}
+void mdq_clear_error() { g_err[0] = '\0'; }
+
+namespace {
+
+mdq_status fail(mdq_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    return mdq_fail(s, "%s", buf);
 }
 
 int storage_bits_m(int layout) {

@@ -20,7 +20,7 @@ CSRC = os.path.join(PKG_ROOT, "csrc")
 INCLUDE = os.path.join(REPO_ROOT, "include")
 LIB_PATH = os.path.join(PKG_DIR, "libmdq.so")
 
-SOURCES = ["mdq_step.cu"]
+SOURCES = ["mdq_step.cu", "mdq_stats.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -169,6 +169,36 @@ def step_multi(items: Sequence[StepItem], p_mode: int = P_FAST,
     run_descs(arr, len(items), dev, p_mode, profile_cycles)
 
 
+def grad_stats(grads: Sequence[torch.Tensor]) -> torch.Tensor:
+    """(sum g, sum g^2, sum |g|, count) per gradient, float64 [len(grads), 4],
+    from one fused pass on the current stream (deterministic).  The scratch
+    workspace is allocated here through torch's caching allocator."""
+    if not grads:
+        return torch.zeros(0, 4, dtype=torch.float64)
+    dev = grads[0].device
+    dt = grads[0].dtype
+    for g in grads:
+        _need_cuda(g, "gradients")
+        _need_contig(g, "gradients")
+        if g.dtype != dt or g.device != dev:
+            raise RuntimeError("gradients of one grad_stats call share dtype and device")
+    if dt not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("gradients must be float32 or bfloat16")
+    n = len(grads)
+    ptrs = (ctypes.c_void_p * n)(*[g.data_ptr() for g in grads])
+    counts = (ctypes.c_int64 * n)(*[g.numel() for g in grads])
+    lib = _lib.load()
+    need = ctypes.c_int64(0)
+    _lib.check(lib.mdq_grad_stats_workspace_bytes(counts, n, ctypes.byref(need)))
+    ws = torch.empty(max(need.value, 8), dtype=torch.uint8, device=dev)
+    out = torch.empty(n, 4, dtype=torch.float64, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.mdq_grad_stats_multi(ptrs, counts, n, _DTYPE_CODE[dt], out.data_ptr(),
+                                      ws.data_ptr(), need.value, _stream_handle(dev))
+    _lib.check(st)
+    return out
+
+
 def layout_for_bits(m_bits: int, v_bits: int) -> int:
     """Storage layout the optimizer uses for a (m_bits, v_bits) pair."""
     if m_bits == v_bits:
@@ -185,5 +215,5 @@ def layout_for_bits(m_bits: int, v_bits: int) -> int:
     return layout_for_bits(b, b)
 
 
-__all__ = ["fused_mdq_adamw", "StepItem", "step_multi", "run_descs", "fill_desc",
+__all__ = ["fused_mdq_adamw", "StepItem", "step_multi", "run_descs", "fill_desc", "grad_stats",
            "layout_for_bits", "P_FAST", "P_EXACT", "LAYOUT_NAMES"]

@@ -179,13 +179,20 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         """Per-parameter [n_l, r_l, v_l] from all-reduced partial sums."""
         sums = torch.zeros(len(self.params), 4, dtype=torch.float64,
                            device=self.flat_grad.device)
-        for pc in self.pieces:
-            _, g = self._piece_views(pc)
-            g64 = g.double()
-            sums[pc.param, 0] += g64.sum()
-            sums[pc.param, 1] += (g64 * g64).sum()
-            sums[pc.param, 2] += g64.abs().sum()
-            sums[pc.param, 3] += pc.n
+        views = [self._piece_views(pc)[1] for pc in self.pieces]
+        if views and self.flat_grad.is_cuda:
+            # One fused pass over every local piece (mdq_grad_stats_multi).
+            part = kernels.grad_stats(views)
+            idx = torch.tensor([pc.param for pc in self.pieces], device=sums.device)
+            sums.index_add_(0, idx, part)
+        else:
+            # The same float64 sums with torch reductions (host tensors).
+            for pc, g in zip(self.pieces, views):
+                g64 = g.double()
+                sums[pc.param, 0] += g64.sum()
+                sums[pc.param, 1] += (g64 * g64).sum()
+                sums[pc.param, 2] += g64.abs().sum()
+                sums[pc.param, 3] += pc.n
         if self.world > 1:
             dist.all_reduce(sums, group=self.group)
         s, s2, sa, cnt = sums.unbind(1)
