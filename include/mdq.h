@@ -164,6 +164,23 @@ mdq_status mdq_grad_stats_multi(const void* const* grads, const int64_t* counts,
                                 int32_t n_tensors, int32_t grad_dtype, double* out,
                                 void* workspace, int64_t workspace_bytes, cudaStream_t stream);
 
+/*
+ * mdq_grad_stats_multi without a caller workspace, for callers that cannot
+ * allocate device memory (a host binding the C ABI directly with no device
+ * allocator of its own, or a step that must not call cudaMalloc, which can
+ * synchronise the device).  No counterpart in the reference.  The scratch is
+ * a fixed 1.5 MiB array inside this library, resident on every GPU that loads
+ * it until the process exits; a call may need at most 65536 partial records,
+ * one per 65536 elements of each tensor (sum over tensors of
+ * ceil(count / 65536)), and larger calls fail with MDQ_ERR_TOO_LARGE.  The
+ * first call on each device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  Calls
+ * share the array: calls that overlap on the GPU race.  Allocates nothing.
+ */
+mdq_status mdq_grad_stats_multi_noalloc(const void* const* grads, const int64_t* counts,
+                                        int32_t n_tensors, int32_t grad_dtype, double* out,
+                                        cudaStream_t stream);
+
 /* Message describing the calling thread's most recent failure ("" if none). */
 const char* mdq_last_error(void);
 

@@ -15,6 +15,7 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <stdarg.h>
+#include <mutex>
 
 #include "mdq.h"
 
@@ -215,3 +216,70 @@ mdq_status mdq_grad_stats_multi(const void* const* grads, const int64_t* counts,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot allocate device memory for the workspace: a host
+// program that binds the C ABI directly (cgo, JNI, ...) and owns no device
+// allocator, or a training step that must not call cudaMalloc (which can
+// synchronise the device) in the middle of its work.  For them the
+// partial-sum records live in a fixed array in this library's device memory:
+// kNoAllocRecords records of three doubles (1.5 MiB), held on every GPU that
+// loads the library until the process exits.  One record covers up to
+// kChunk = 65536 elements of one tensor, so a call accepts at most
+// kNoAllocRecords records in total (sum over tensors of ceil(count / 65536),
+// about 4.29e9 elements when tensors are large).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocRecords = 65536;
+static __device__ __align__(256) double g_noalloc_partials[kNoAllocRecords * 3];
+
+// Device address of g_noalloc_partials per device.  The host-side name of the
+// array is only a stand-in; its device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+mdq_status noalloc_scratch(void** ptr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return mdq_fail(MDQ_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return mdq_fail(MDQ_ERR_CUDA, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* a = nullptr;
+        e = cudaGetSymbolAddress(&a, g_noalloc_partials);
+        if (e != cudaSuccess || a == nullptr)
+            return mdq_fail(MDQ_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_noalloc_addr[dev] = a;
+    }
+    *ptr = g_noalloc_addr[dev];
+    return MDQ_OK;
+}
+
+}  // namespace
+
+extern "C" mdq_status mdq_grad_stats_multi_noalloc(const void* const* grads, const int64_t* counts,
+                                                   int32_t n_tensors, int32_t grad_dtype,
+                                                   double* out, cudaStream_t stream) {
+    mdq_clear_error();
+    int64_t need = 0;
+    mdq_status st = mdq_grad_stats_workspace_bytes(counts, n_tensors, &need);
+    if (st != MDQ_OK) return st;
+    const int64_t cap = kNoAllocRecords * 3 * (int64_t)sizeof(double);
+    if (need > cap)
+        return mdq_fail(MDQ_ERR_TOO_LARGE,
+                        "mdq_grad_stats_multi_noalloc: %lld partial records needed, the built-in "
+                        "scratch holds %lld (one per 65536 elements of each tensor)",
+                        (long long)(need / (3 * (int64_t)sizeof(double))),
+                        (long long)kNoAllocRecords);
+    void* scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st != MDQ_OK) return st;
+    // Every record pass 2 reads is written by pass 1 of the same call, so the
+    // scratch needs no clearing; calls that overlap on the GPU share it and race.
+    return mdq_grad_stats_multi(grads, counts, n_tensors, grad_dtype, out, scratch, cap, stream);
+}
+

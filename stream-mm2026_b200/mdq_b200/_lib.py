@@ -91,6 +91,10 @@ _SIGNATURES = {
                                             ctypes.POINTER(ctypes.c_int64), ctypes.c_int32,
                                             ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_int64, ctypes.c_void_p]),
+    "mdq_grad_stats_multi_noalloc": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p),
+                                                    ctypes.POINTER(ctypes.c_int64), ctypes.c_int32,
+                                                    ctypes.c_int32, ctypes.c_void_p,
+                                                    ctypes.c_void_p]),
     "mdq_last_error": (ctypes.c_char_p, []),
     "mdq_abi_version": (ctypes.c_int32, []),
 }
