@@ -1,0 +1,93 @@
+"""ZeRO-1 on real GPUs with NCCL (needs >= 2 devices; skipped otherwise):
+reduce-scatter / fused step / all-gather equals the unsharded optimizer on one
+GPU with the averaged gradients, bit for bit (fixed bit widths, exact p)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [1000, 3, (1 << 20) + 17, 256, 777, 2048, 1, 65536 * 3 + 5]
+
+
+def _grads(rank, step):
+    g = torch.Generator().manual_seed(1000 * step + rank)
+    return [torch.round(torch.randn(n, generator=g) * 1024 * 2.0 ** (i % 3)) / 2 ** 20
+            for i, n in enumerate(SIZES)]
+
+
+def _params(device):
+    g = torch.Generator().manual_seed(0)
+    return [torch.nn.Parameter((torch.randn(n, generator=g) * 0.02).to(device)) for n in SIZES]
+
+
+KW = dict(lr=1e-3, weight_decay=0.01, block_size=256, p_mode="exact")
+
+
+def _worker(rank, world, port, steps, bits, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        from mdq_b200.zero1 import ZeroMDQAdamW
+
+        params = _params(torch.device("cuda", rank))
+        opt = ZeroMDQAdamW([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
+                           fixed_bits=bits, **KW)
+        for t in range(1, steps + 1):
+            opt.zero_grad()
+            for p, g in zip(params, _grads(rank, t)):
+                p.grad.copy_(g)
+            opt.step()
+        torch.cuda.synchronize()
+        sd = opt.consolidated_state_dict()
+        if rank == 0:
+            q.put(([p.detach().cpu().numpy() for p in params],
+                   {i: {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in st.items()}
+                    for i, st in sd["state"].items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("bits", [4, (8, 4), 8])
+def test_zero1_nccl_equals_unsharded(cuda_device, bits):
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    from mdq_b200.optim import MDQAdamWSimpleFusedIO
+
+    steps = 4
+    params = _params(cuda_device)
+    opt = MDQAdamWSimpleFusedIO([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
+                                fixed_bits=bits, **KW)
+    for t in range(1, steps + 1):
+        per = [_grads(r, t) for r in range(world)]
+        for i, p in enumerate(params):
+            p.grad = (sum(pr[i] for pr in per) / world).to(cuda_device)
+        opt.step()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, bits, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got_params, state = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for i, (a, b) in enumerate(zip(params, got_params)):
+        np.testing.assert_array_equal(a.detach().cpu().numpy().view(np.int32), b.view(np.int32),
+                                      err_msg=f"param {i}")
+        rs = opt.state[a]
+        for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
+            np.testing.assert_array_equal(rs[k].cpu().numpy().view(np.uint8),
+                                          state[i][k].view(np.uint8), err_msg=f"param {i} {k}")
