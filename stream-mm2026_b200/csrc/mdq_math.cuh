@@ -24,6 +24,7 @@ struct StepConsts {
     float sqrt_bc2;            // sqrtf(1 - beta2^step)    (IEEE sqrt)
     float inv_sqrt_bc2;        // 1 / sqrt_bc2             (fast p mode only)
     float lm_f, lv_f;          // (float)2^(m_bits-1), (float)(2^v_bits - 1)
+    float inv_lm;              // 2^-(m_bits-1), exact
     double lm_d, lv_d;         // the same levels in double, for clamping
 };
 
@@ -48,6 +49,7 @@ __device__ __forceinline__ StepConsts make_step_consts(float b1, float b2, float
     c.lv_d = pow(2.0, v_bits) - 1.0;
     c.lm_f = (float)c.lm_d;
     c.lv_f = (float)c.lv_d;
+    c.inv_lm = (float)(1.0 / c.lm_d);
     return c;
 }
 
@@ -88,8 +90,17 @@ __device__ __forceinline__ float update_p(float w, float m, float v, const StepC
 __device__ __forceinline__ float log_v_of(float v) { return logf(__fadd_rn(v, 1e-12f)); }
 
 // New block scales from the block reductions (CUDA/stquant_kernel.cu:192-195).
+// Division by the power of two 2^(m_bits-1) is exact scaling, identical to the
+// multiplication by its exact reciprocal.
 __device__ __forceinline__ float scale_m_of(float max_abs_m, const StepConsts& c) {
-    return __fdiv_rn(__fadd_rn(max_abs_m, 1e-12f), c.lm_f);
+    return __fmul_rn(__fadd_rn(max_abs_m, 1e-12f), c.inv_lm);
+}
+
+// Reciprocal estimate; the codes are verified exactly whatever its error.
+__device__ __forceinline__ float rcp_estimate(float d) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+    return r;
 }
 __device__ __forceinline__ float scale_v_of(float max_lv, float min_lv, const StepConsts& c) {
     return __fdiv_rn(__fadd_rn(__fsub_rn(max_lv, min_lv), 1e-12f), c.lv_f);

@@ -253,7 +253,7 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
 
     // ---- requantise (CUDA/stquant_kernel.cu:204-216) --------------------
     const float dm = __fadd_rn(new_sm, 1e-12f), dv = __fadd_rn(new_sv, 1e-12f);
-    const float rdm = __frcp_rn(dm), rdv = __frcp_rn(dv);
+    const float rdm = rcp_estimate(dm), rdv = rcp_estimate(dv);
     const float half_dm = 0.5f * dm, half_dv = 0.5f * dv;
     // v codes from the approximate log see X' = RN(a - lmin) instead of the
     // reference's X = RN(logf(x) - lmin): |X' - X| <= log_tol + one ulp of a
