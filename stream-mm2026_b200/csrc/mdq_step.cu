@@ -46,6 +46,9 @@ constexpr int kCapSmall = 8;                  // descriptors per launch, small t
 constexpr int kCapLarge = 224;                // descriptors per launch, large table
 constexpr int kProfSlots = 5;
 
+#ifndef MDQ_USE_REDUX
+#define MDQ_USE_REDUX 1
+#endif
 #ifndef MDQ_MIN_CTAS_PER_SM
 #define MDQ_MIN_CTAS_PER_SM 3
 #endif
@@ -94,8 +97,9 @@ __device__ int find_desc(const LaunchParams<CAP>& P, int tile) {
 // one shared-memory exchange when a block spans several warps.  Every step is
 // an fmaxf / fminf, which skip NaNs as the reference's reduction does.
 template <unsigned MAXMASK, int NV>
-__device__ __forceinline__ void group_reduce(float (&x)[NV], int gthreads, float (*red)[kWarps]) {
-    if (gthreads >= 32) {
+__device__ __forceinline__ void group_reduce(float (&x)[NV], int gthreads, float4* red) {
+    static_assert(NV <= 4, "partials are exchanged as one float4 per warp");
+    if (MDQ_USE_REDUX && gthreads >= 32) {
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
             float r;
@@ -120,18 +124,22 @@ __device__ __forceinline__ void group_reduce(float (&x)[NV], int gthreads, float
     if (gthreads > 32) {
         const int w = threadIdx.x >> 5;
         if ((threadIdx.x & 31) == 0) {
-#pragma unroll
-            for (int k = 0; k < NV; ++k) red[k][w] = x[k];
+            float4 v;
+            v.x = x[0];
+            v.y = NV > 1 ? x[1 % NV] : 0.0f;
+            v.z = NV > 2 ? x[2 % NV] : 0.0f;
+            v.w = NV > 3 ? x[3 % NV] : 0.0f;
+            red[w] = v;
         }
         __syncthreads();
         const int wpg = gthreads >> 5;
         const int w0 = (w / wpg) * wpg;
+        for (int i = 0; i < wpg; ++i) {
+            const float4 v = red[w0 + i];
+            const float vals[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            float r = red[k][w0];
-            for (int i = 1; i < wpg; ++i)
-                r = ((MAXMASK >> k) & 1u) ? fmaxf(r, red[k][w0 + i]) : fminf(r, red[k][w0 + i]);
-            x[k] = r;
+            for (int k = 0; k < NV; ++k)
+                x[k] = ((MAXMASK >> k) & 1u) ? fmaxf(x[k], vals[k]) : fminf(x[k], vals[k]);
         }
     }
 }
@@ -148,7 +156,7 @@ __device__ __forceinline__ void prof_mark(unsigned long long (&pc)[kProfSlots], 
 // `red` is this tile's reduction scratch.
 template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL>
 __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
-                                          float (*red)[kWarps],
+                                          float4* red,
                                           unsigned long long (&pc)[kProfSlots],
                                           unsigned long long& t0) {
     using CI = Codes<LAYOUT>;
@@ -319,7 +327,7 @@ template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP>
 __global__ void __launch_bounds__(kThreads, MDQ_MIN_CTAS_PER_SM)
 mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
     using CI = Codes<LAYOUT>;
-    __shared__ float s_red[2][3][kWarps];  // alternates by tile
+    __shared__ float4 s_red[2][kWarps];  // per-warp partials, alternating by tile
     __shared__ TileCtx s_ctx;
 
     const int tid = threadIdx.x;
@@ -351,7 +359,7 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
         const int64_t n = s_ctx.n;
         const int64_t tile_e0 = (int64_t)(tile - s_ctx.tile_begin) << kLogTile;
 
-        float (*red)[kWarps] = s_red[tile & 1];
+        float4* red = s_red[tile & 1];
         if (s_ctx.vec && tile_e0 + kTile <= n)
             tile_body<LAYOUT, GT, EXACT_P, PROF, true>(s_ctx, tile_e0, red, pc, t0);
         else
