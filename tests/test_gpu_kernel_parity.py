@@ -47,6 +47,8 @@ CASES = [
     ("packed4", 4, 1, 256),
     ("packed4", 4, 127, 32),
     ("packed4", 4, 5000, 8),
+    ("packed4", 4, 70_001, 16),
+    ("s8u8", 8, 140_003, 1024),
     ("s8u8", 8, 1 << 20, 256),
     ("s8u8", 8, 70_001, 1024),
     ("s8u8", 8, 70_001, 512),
