@@ -38,10 +38,14 @@
 
 namespace mdq {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+// Every launch walks 2048-element tiles: 256 threads x 8 elements (PT = 8,
+// 3 CTAs per SM) or 128 threads x 16 elements (PT = 16, 4 CTAs per SM).
+template <int PT> constexpr int threads_for() { return PT == 16 ? 128 : 256; }
+constexpr int kThreads = 256;                  // PT = 8 CTA size
+constexpr int kWarps = kThreads / 32;          // warps of the largest CTA
 constexpr int kPerThread = 8;
-constexpr int kTile = kThreads * kPerThread;  // 2048 elements (PT = 8); PT = 16 doubles it
+constexpr int kTile = kThreads * kPerThread;  // 2048 elements for both shapes
+constexpr int kLogTile = 11;
 constexpr int kCapSmall = 8;                  // descriptors per launch, small table
 constexpr int kCapLarge = 224;                // descriptors per launch, large table
 constexpr int kProfSlots = 5;
@@ -53,7 +57,7 @@ constexpr int kProfSlots = 5;
 #define MDQ_ENABLE_PT16 1
 #endif
 #ifndef MDQ_MIN_CTAS_PT16
-#define MDQ_MIN_CTAS_PT16 2
+#define MDQ_MIN_CTAS_PT16 4
 #endif
 #ifndef MDQ_MIN_CTAS_PER_SM
 #define MDQ_MIN_CTAS_PER_SM 3
@@ -350,10 +354,10 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
 // several warps, inside the block reduction.
 // ---------------------------------------------------------------------------
 template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT>
-__global__ void __launch_bounds__(kThreads, PT == 8 ? MDQ_MIN_CTAS_PER_SM : MDQ_MIN_CTAS_PT16)
+__global__ void __launch_bounds__(threads_for<PT>(), PT == 8 ? MDQ_MIN_CTAS_PER_SM : MDQ_MIN_CTAS_PT16)
 mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
-    constexpr int kTileT = kThreads * PT;
-    constexpr int kLogTileT = PT == 8 ? 11 : 12;
+    constexpr int kTileT = kTile;
+    constexpr int kLogTileT = kLogTile;
     using CI = Codes<LAYOUT>;
     __shared__ float4 s_red[2][kWarps];  // per-warp partials, alternating by tile
     __shared__ TileCtx s_ctx;
@@ -637,9 +641,9 @@ mdq_status device_sms(int* sms) {
 }
 
 template <typename K>
-int blocks_per_sm(K kernel) {
+int blocks_per_sm(K kernel, int threads) {
     int b = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, mdq::kThreads, 0) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, 0) != cudaSuccess ||
         b < 1)
         b = 1;
     return b;
@@ -649,10 +653,11 @@ template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT>
 mdq_status launch_tiles_t(const mdq::LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
     auto k = mdq::mdq_step_tiles<LAYOUT, GT, EXACT_P, PROF, CAP, PT>;
     static int occ = 0;  // per instantiation; identical across B200 devices
-    if (occ == 0) occ = blocks_per_sm(k);
+    constexpr int kNT = mdq::threads_for<PT>();
+    if (occ == 0) occ = blocks_per_sm(k, kNT);
     int grid = sms * occ;
     if (grid > P.total_tiles) grid = P.total_tiles;
-    k<<<grid, mdq::kThreads, 0, stream>>>(P);
+    k<<<grid, kNT, 0, stream>>>(P);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(MDQ_ERR_CUDA, "step launch: %s", cudaGetErrorString(e));
     return MDQ_OK;
@@ -754,7 +759,7 @@ mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bo
     const int pt = MDQ_ENABLE_PT16 && ((v4 && min_block >= 16) ||
                                        (layout == MDQ_LAYOUT_S8U8 && min_block >= 1024))
                        ? 16 : 8;
-    const int64_t tile = (int64_t)mdq::kThreads * pt;
+    const int64_t tile = mdq::kTile;
     int i = 0;
     while (i < count) {
         P.n_desc = 0;
