@@ -25,6 +25,19 @@ namespace mdq {
 constexpr int kMagicBits = 0x4B400000;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 
+// Low bytes of four words packed into one word (PRMT).
+__device__ __forceinline__ unsigned pack_low_bytes(unsigned a, unsigned b, unsigned c, unsigned d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Magic word of (16 * qhi + qlo + bias) from the magic words of qhi and qlo,
+// in float arithmetic (exact: every intermediate is an integer below 2^22
+// offset by the magic constant).  Its low byte is the packed nibble pair.
+__device__ __forceinline__ unsigned nibble_pair(int hi_word, int lo_word, float bias) {
+    const float rhi = __fsub_rn(__int_as_float(hi_word), kMagic);
+    return (unsigned)__float_as_int(__fmaf_rn(rhi, 16.0f, __fadd_rn(__int_as_float(lo_word), bias)));
+}
+
 // Exact float of a small integer (|q| < 2^22) without an I2F instruction.
 __device__ __forceinline__ float small_int_to_float(int q) {
     return __fsub_rn(__int_as_float(kMagicBits + q), kMagic);
@@ -68,14 +81,14 @@ template <> struct Codes<MDQ_LAYOUT_PACKED4> {
     __device__ static unsigned byte_of(int mw, int vw) {
         return (((unsigned)vw & 15u) << 4) | (((unsigned)mw + 8u) & 15u);
     }
+    // Byte = 16 q_v + (q_m + 8), formed in float arithmetic and gathered with
+    // byte permutes (magic words keep every value exact).
     __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
-        unsigned lo = 0, hi = 0;
+        unsigned b[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            lo |= byte_of(mw[j], vw[j]) << (8 * j);
-            hi |= byte_of(mw[j + 4], vw[j + 4]) << (8 * j);
-        }
-        __stcs(reinterpret_cast<uint2*>(static_cast<uint8_t*>(t.m) + e), make_uint2(lo, hi));
+        for (int j = 0; j < 8; ++j) b[j] = nibble_pair(vw[j], mw[j], 8.0f);
+        __stcs(reinterpret_cast<uint2*>(static_cast<uint8_t*>(t.m) + e),
+               make_uint2(pack_low_bytes(b[0], b[1], b[2], b[3]), pack_low_bytes(b[4], b[5], b[6], b[7])));
     }
     __device__ static void store1(const TensorPtrs& t, int64_t e, int mw, int vw) {
         static_cast<uint8_t*>(t.m)[e] = (uint8_t)byte_of(mw, vw);
@@ -113,12 +126,8 @@ template <typename MT, typename VT, bool MAGIC> struct CodesPlain {
     template <typename T>
     __device__ static void st8(T* dst, const int (&o)[8]) {
         if constexpr (sizeof(T) == 1) {
-            unsigned lo = 0, hi = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                lo |= ((unsigned)o[j] & 0xffu) << (8 * j);
-                hi |= ((unsigned)o[j + 4] & 0xffu) << (8 * j);
-            }
+            const unsigned lo = pack_low_bytes(o[0], o[1], o[2], o[3]);
+            const unsigned hi = pack_low_bytes(o[4], o[5], o[6], o[7]);
             __stcs(reinterpret_cast<uint2*>(dst), make_uint2(lo, hi));
         } else if constexpr (sizeof(T) == 2) {
             uint4 w;
@@ -186,14 +195,11 @@ template <> struct Codes<MDQ_LAYOUT_M8V4> {
         qv = (int)((static_cast<const uint8_t*>(t.v)[e >> 1] >> (4 * (e & 1))) & 15u);
     }
     __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
-        unsigned lo = 0, hi = 0, nib = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            lo |= ((unsigned)mw[j] & 0xffu) << (8 * j);
-            hi |= ((unsigned)mw[j + 4] & 0xffu) << (8 * j);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) nib |= ((unsigned)vw[j] & 15u) << (4 * j);
+        const unsigned lo = pack_low_bytes(mw[0], mw[1], mw[2], mw[3]);
+        const unsigned hi = pack_low_bytes(mw[4], mw[5], mw[6], mw[7]);
+        // v codes are within [0, 15] (4-bit levels), so pairs pack exactly.
+        const unsigned nib = pack_low_bytes(nibble_pair(vw[1], vw[0], 0.0f), nibble_pair(vw[3], vw[2], 0.0f),
+                                            nibble_pair(vw[5], vw[4], 0.0f), nibble_pair(vw[7], vw[6], 0.0f));
         __stcs(reinterpret_cast<uint2*>(static_cast<int8_t*>(t.m) + e), make_uint2(lo, hi));
         __stcs(reinterpret_cast<unsigned*>(static_cast<uint8_t*>(t.v) + (e >> 1)), nib);
     }

@@ -194,11 +194,15 @@ __device__ __forceinline__ int round_checked(float y, float x, float d, float ha
 //    a code is taken from the approximation only when it clears its rounding
 //    boundary by more than that error, otherwise from logf itself.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float approx_ln(float x) {
+constexpr float kLn2 = 0.693147182f;
+
+__device__ __forceinline__ float approx_log2(float x) {
     float l2;
     asm("lg2.approx.f32 %0, %1;" : "=f"(l2) : "f"(x));
-    return __fmul_rn(l2, 0.693147182f);
+    return l2;
 }
+
+__device__ __forceinline__ float approx_ln(float x) { return __fmul_rn(approx_log2(x), kLn2); }
 
 __device__ __forceinline__ float log_tol(float a) {
     return __fmaf_rn(fabsf(a), 0x1p-21f, 0x1p-20f);

@@ -291,10 +291,13 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     // reference's X = RN(logf(x) - lmin): |X' - X| <= log_tol + one ulp of a
     // difference of at most max(lmax - lmin, 1) (logs of floats >= 1e-12 lie
     // in [-27.7, 88.8]).  The remainder test absorbs that error.
+    // X' is formed as RN(lg2(x) * ln2 - lmin) in one FMA: against the checked
+    // a = RN(lg2(x) * ln2) that adds at most half an ulp of a, |a| 2^-24.
     float thr_v = half_dv;
     if (kApprox) {
+        const float amax = fmaxf(fabsf(lmax), fabsf(lmin));
         const float errx = __fmaf_rn(fmaxf(__fsub_rn(lmax, lmin), 1.0f), 0x1p-22f,
-                                     log_tol(fmaxf(fabsf(lmax), fabsf(lmin))));
+                                     __fmaf_rn(amax, 0x1p-23f, log_tol(amax)));
         // (less one relative 2^-22 of d/2 for the rounding of the remainder)
         thr_v = __fmaf_rn(-errx, 1.001f, __fmul_rn(half_dv, 1.0f - 0x1p-22f));
     }
@@ -312,7 +315,8 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
         float r;
         mw[j] = min(round_checked<kCorrect>(__fmul_rn(m[j], rdm), m[j], dm, half_dm, r), mw_hi);
         rem_m = max_nan(rem_m, r);
-        const float xv = __fsub_rn(kApprox ? approx_ln(x[j]) : logf(x[j]), lmin);
+        const float xv = kApprox ? __fmaf_rn(approx_log2(x[j]), kLn2, -lmin)
+                                 : __fsub_rn(logf(x[j]), lmin);
         vw[j] = round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
         rem_v = max_nan(rem_v, r);
     }
@@ -324,7 +328,8 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
             float r;
             round_checked<kCorrect>(__fmul_rn(m[j], rdm), m[j], dm, half_dm, r);
             if (!kMagicC || !(r < half_dm)) mw[j] = CI::m_word(requant_m_ref(m[j], dm, C.lm_d));
-            const float xv = __fsub_rn(kApprox ? approx_ln(x[j]) : logf(x[j]), lmin);
+            const float xv = kApprox ? __fmaf_rn(approx_log2(x[j]), kLn2, -lmin)
+                                 : __fsub_rn(logf(x[j]), lmin);
             round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
             if (!kMagicC || !(r < thr_v))
                 vw[j] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[j]), lmin), dv, C.lv_d));
