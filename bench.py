@@ -270,6 +270,60 @@ def run_e2e(args, device, p, grad, codes, sm, sv, vmin, t0):
     return (time.perf_counter() - t_start) / steps
 
 
+def gpt2_medium_shapes():
+    """Parameter shapes of GPT-2 medium (24 layers, d=1024, 16 heads, vocab 50257,
+    ctx 1024, tied embeddings): 355M parameters."""
+    d, v, ctx, layers = 1024, 50257, 1024, 24
+    shapes = [(v, d), (ctx, d)]
+    for _ in range(layers):
+        shapes += [(d,), (d,), (d, 3 * d), (3 * d,), (d, d), (d,), (d,), (d,),
+                   (d, 4 * d), (4 * d,), (4 * d, d), (d,)]
+    shapes += [(d,), (d,)]
+    return shapes
+
+
+def run_zero1(args, rank, world, device):
+    """ZeRO-1 step on N GPUs (BASELINE config 4 shapes and precision): bf16
+    gradients reduce-scattered over NCCL, the fused 8-bit-m / 4-bit-v step on
+    each rank's shard, fp32 parameters all-gathered in place.  Device time of
+    the whole optimizer.step(), max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from mdq_b200.zero1 import ZeroMDQAdamW
+
+    g = torch.Generator(device=device).manual_seed(rank)
+    params = [torch.nn.Parameter(torch.randn(sh, device=device, generator=g) * 0.02)
+              for sh in gpt2_medium_shapes()]
+    n = sum(p.numel() for p in params)
+    opt = ZeroMDQAdamW(params, lr=1e-3, weight_decay=0.01, block_size=256, fixed_bits=(8, 4),
+                       p_mode="fast", grad_dtype=torch.bfloat16)
+    opt.flat_grad.normal_(0, 1e-3, generator=g)
+    for _ in range(3):
+        opt.step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    steps = max(5, min(args.steps, 20))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        opt.step()
+    b.record()
+    torch.cuda.synchronize()
+    x = torch.tensor([a.elapsed_time(b) / steps], device=device)
+    dist.all_reduce(x, op=dist.ReduceOp.MAX)
+    ms = float(x.item())
+    total = opt.layout.total
+    link_bytes = (world - 1) * total // world * (2 + 4)   # RS of bf16 + AG of fp32, per GPU out
+    return {"model": "gpt2-medium shapes (355M params)", "params": n, "m_bits": 8, "v_bits": 4,
+            "block": 256, "grad_dtype": "bf16", "ms_per_step": round(ms, 3),
+            "gparams_per_s": round(n / (ms * 1e-3) / 1e9, 2),
+            "nvlink_bytes_per_gpu_per_step": link_bytes,
+            "nvlink_gbs_per_gpu": round(link_bytes / (ms * 1e-3) / 1e9, 1),
+            "what": "optimizer.step(): reduce-scatter(avg) bf16 grads + fused step on the "
+                    "shard + all-gather fp32 params (NCCL), device time, max over ranks"}
+
+
 def traffic_per_launch(n_elems):
     """DRAM bytes per launch from the committed ncu summary of this kernel,
     scaled from its capture size to this launch (traffic is proportional)."""
@@ -369,6 +423,7 @@ def main() -> int:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     ms, ms_exact, clocks, e2e = run_ours(args, rank, world, local_rank)
+    zero1 = run_zero1(args, rank, world, torch.device("cuda", local_rank)) if world > 1 else None
     n = 1 << LOG2_N
     value = world * n / (ms * 1e-3) / 1e9
     bytes_launch = n * BYTES_PER_ELEM
@@ -392,6 +447,8 @@ def main() -> int:
                              "ms_per_step": round(ms_exact, 4)},
             "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
         }
+        if zero1 is not None:
+            line["zero1"] = zero1
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

@@ -114,6 +114,8 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             n = p.numel()
             self.flat_param[off:off + n].copy_(p.detach().reshape(-1))
             p.data = self.flat_param[off:off + n].view_as(p)
+            if grad_dtype != p.dtype and hasattr(p, "grad_dtype"):
+                p.grad_dtype = grad_dtype  # low-precision gradients of fp32 parameters
             p.grad = self.flat_grad[off:off + n].view_as(p)
         self.pieces = self.layout.pieces(self.rank)
         s = self.layout.shard
