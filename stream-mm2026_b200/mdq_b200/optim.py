@@ -367,8 +367,23 @@ class MDQAdamWSimple(Optimizer):
             self.v_global_ema = stats["v_global_ema"]
             self.total_steps = stats["total_steps"]
         super().load_state_dict(state_dict)
-        # Optimizer.load_state_dict casts floating state to the param dtype and
-        # leaves integer codes as saved, which is the layout the step expects.
+        # Optimizer.load_state_dict casts every state tensor of a floating-point
+        # parameter to the parameter's dtype, codes included (uint32 codes of
+        # the 32-bit layout do not even survive a float32 round trip).  The
+        # reference (CUDA/stquant_opt_simple.py:371-378) inherits that cast and
+        # its next step then finds float storage it cannot dispatch; here the
+        # saved integer code tensors are put back as they were saved.
+        saved = state_dict["state"]
+        ids = [i for g in state_dict["param_groups"] for i in g["params"]]
+        params = [p for g in self.param_groups for p in g["params"]]
+        for pid, p in zip(ids, params):
+            src, dst = saved.get(pid), self.state.get(p)
+            if src is None or dst is None:
+                continue
+            for key in ("exp_avg", "exp_avg_sq"):
+                t = src.get(key)
+                if torch.is_tensor(t) and not t.dtype.is_floating_point:
+                    dst[key] = t.to(p.device, copy=True)
 
     def dequantized_moments(self, p):
         """Float m and v of one parameter, decoded from its codes and scales."""

@@ -286,6 +286,52 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         self._all_gather_params()
         return loss
 
+    def load_consolidated_state_dict(self, state_dict):
+        """Load an unsharded state (from ``consolidated_state_dict``, at any
+        world size, or from an unsharded MDQ optimizer's ``state_dict``): each
+        rank keeps the slices of codes and scales that fall in its pieces.
+        Parameters themselves are restored by the caller (model state)."""
+        saved = state_dict["state"]
+        for g, sg in zip(self.param_groups, state_dict["param_groups"]):
+            for k, v in sg.items():
+                if k != "params":
+                    g[k] = v
+        stats = state_dict.get("mdq_global_stats")
+        if stats is not None:
+            self.n_ema, self.r_ema = stats["n_ema"], stats["r_ema"]
+            self.v_global_ema, self.total_steps = stats["v_global_ema"], stats["total_steps"]
+        held = {pc.param: pc for pc in self.pieces}
+        B = self.block
+        self.state.clear()
+        for i, p in enumerate(self.params):
+            src = saved.get(i)
+            if src is None:
+                continue
+            bits = int(src["current_bit"])
+            st = self.state[p]
+            st["step"] = int(src["step"])
+            st["current_bit"] = bits
+            st["last_score"] = torch.as_tensor(src["last_score"]).to(p.device, torch.float32)
+            st["_layout_bits"] = bits
+            pc = held.get(i)
+            if pc is None:
+                continue
+            ea, easq = src["exp_avg"], src["exp_avg_sq"]
+            a, n = pc.start, pc.n
+            st["exp_avg"] = ea[a:a + n].to(p.device, copy=True)
+            if easq.numel() == 0:
+                st["exp_avg_sq"] = easq.to(p.device, copy=True)
+            elif easq.numel() == ea.numel():
+                st["exp_avg_sq"] = easq[a:a + n].to(p.device, copy=True)
+            else:  # two v codes per byte
+                if a % 2:
+                    raise ValueError("nibble-packed v codes need an even block size")
+                st["exp_avg_sq"] = easq[a // 2:a // 2 + (n + 1) // 2].to(p.device, copy=True)
+            b0, nb = a // B, -(-n // B)
+            for k in ("scale_m", "scale_v", "v_min"):
+                st[k] = src[k][b0:b0 + nb].to(p.device, torch.float32, copy=True)
+            st["piece"] = (a, n)
+
     # ------------------------------------------------------------------
     def consolidated_state_dict(self):
         """The unsharded per-parameter state (reference layout) on every rank:

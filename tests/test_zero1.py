@@ -140,3 +140,94 @@ def test_sharded_step_equals_unsharded(world, kw):
             a = rs[k].numpy()
             np.testing.assert_array_equal(a.view(np.uint8), st[k].view(np.uint8),
                                           err_msg=f"param {i} {k}")
+
+
+def _resume_worker(rank, world, port, sizes, kw, phase, payload, q):
+    """Phase "save": steps 1-6, then rank 0 returns params + consolidated
+    state.  Phase "resume": load them (at this world size) and run steps 7-11.
+    Every rank sees the same gradients, so the result is world-independent."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _use_oracle()
+        from mdq_b200.zero1 import ZeroMDQAdamW
+
+        torch.set_num_threads(1)
+        params = _params(sizes)
+        if phase == "resume":
+            for p, v in zip(params, payload[0]):
+                p.data.copy_(torch.from_numpy(v))
+        opt = ZeroMDQAdamW([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
+                           lr=1e-3, weight_decay=0.01, block_size=256, **kw)
+        steps = range(1, 7)
+        if phase == "resume":
+            opt.load_consolidated_state_dict(_torch_tree(payload[1]))
+            steps = range(7, 12)
+        for t in steps:
+            opt.zero_grad()
+            for p, g in zip(params, _grads(0, t, sizes)):
+                p.grad.copy_(g)
+            opt.step()
+        sd = _np_tree(opt.consolidated_state_dict())
+        if rank == 0:
+            q.put(([p.detach().numpy().copy() for p in params], sd))
+    finally:
+        dist.destroy_process_group()
+
+
+def _np_tree(x):
+    # Queues pickle tensors through torch's sharing path, which mishandles
+    # uint16/uint32 storage; states travel as numpy.
+    if torch.is_tensor(x):
+        return ("__t", x.detach().cpu().numpy())
+    if isinstance(x, dict):
+        return {k: _np_tree(v) for k, v in x.items()}
+    if isinstance(x, list):
+        return [_np_tree(v) for v in x]
+    return x
+
+
+def _torch_tree(x):
+    if isinstance(x, tuple) and len(x) == 2 and x[0] == "__t":
+        return torch.from_numpy(x[1])
+    if isinstance(x, dict):
+        return {k: _torch_tree(v) for k, v in x.items()}
+    if isinstance(x, list):
+        return [_torch_tree(v) for v in x]
+    return x
+
+
+def _spawn(world, *args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_resume_worker, args=(r, world, port) + args + (q,))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return out
+
+
+@pytest.mark.parametrize("w_save,w_resume,kw", [(2, 3, dict(fixed_bits=(8, 4))), (3, 2, dict())])
+def test_checkpoint_resharding_resume(w_save, w_resume, kw):
+    """Save a consolidated state at one world size, resume at another: the
+    continued run equals an unsharded run of all eleven steps bit for bit."""
+    sizes = SIZES if kw else [n for n in SIZES if n > 1]
+    ref_params, ref_opt = _unsharded(1, 11, kw, sizes)
+    saved = _spawn(w_save, sizes, kw, "save", None)
+    params, sd = _spawn(w_resume, sizes, kw, "resume", saved)
+    sd = _torch_tree(sd)
+    for i, (a, b) in enumerate(zip(ref_params, params)):
+        np.testing.assert_array_equal(a.detach().numpy().view(np.int32), b.view(np.int32),
+                                      err_msg=f"param {i}")
+    for i, p in enumerate(ref_params):
+        rs, st = ref_opt.state[p], sd["state"][i]
+        assert st["step"] == rs["step"] and st["current_bit"] == rs["current_bit"], i
+        for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
+            np.testing.assert_array_equal(rs[k].numpy().view(np.uint8),
+                                          st[k].numpy().view(np.uint8), err_msg=f"param {i} {k}")
