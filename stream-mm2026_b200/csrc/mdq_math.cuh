@@ -160,6 +160,18 @@ __device__ __noinline__ double requant_v_ref(float x, float d, double lv) {
 // y = x * RN(1/d) can be off by more than the distance to a half-integer).
 // A NaN operand gives a NaN remainder, which fails every comparison.
 // ---------------------------------------------------------------------------
+// Three-input max / min (sm_100): NaN operands are skipped as by fmaxf / fminf.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 __device__ __forceinline__ float max_nan(float a, float b) {
     float r;
     asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
@@ -196,9 +208,11 @@ __device__ __forceinline__ int round_checked(float y, float x, float d, float ha
 // ---------------------------------------------------------------------------
 constexpr float kLn2 = 0.693147182f;
 
+// Flush-to-zero form: every argument here is a normal float >= 1e-12 (or NaN),
+// where it equals the non-flushing one and needs no subnormal scaling.
 __device__ __forceinline__ float approx_log2(float x) {
     float l2;
-    asm("lg2.approx.f32 %0, %1;" : "=f"(l2) : "f"(x));
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(l2) : "f"(x));
     return l2;
 }
 

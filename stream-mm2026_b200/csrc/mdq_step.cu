@@ -59,6 +59,9 @@ constexpr int kProfSlots = 5;
 #ifndef MDQ_MIN_CTAS_PT16
 #define MDQ_MIN_CTAS_PT16 4
 #endif
+#ifndef MDQ_USE_TABLES
+#define MDQ_USE_TABLES 1
+#endif
 #ifndef MDQ_MIN_CTAS_PER_SM
 #define MDQ_MIN_CTAS_PER_SM 3
 #endif
@@ -161,10 +164,51 @@ __device__ __forceinline__ void prof_mark(unsigned long long (&pc)[kProfSlots], 
     t0 = t1;
 }
 
+// Dequantisation by table for 4-bit codes.  A 4-bit code has 16 values, so
+// the 16 dequantised values of a block (v = expf(fma(q, sv, v_min)),
+// m = q * sm: CUDA/stquant_kernel.cu:163-165) are computed once, entry k by
+// lane k of each 16-lane half-warp, and every element fetches its value with
+// one 16-wide shuffle indexed by the code's nibble (a 16-wide shuffle reads
+// only the low four bits of the index, so the nibble needs no mask).  Every
+// lane of a half-warp must lie in the same block: blocks of >= 16 * PT.
+template <int LAYOUT> struct TableCodes;
+template <> struct TableCodes<MDQ_LAYOUT_PACKED4> {
+    struct Raw { uint2 w; };
+    __device__ static void load8(const TensorPtrs& t, int64_t e, Raw& r) {
+        r.w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(t.m) + e));
+    }
+    // Byte j: q_m + 8 in the low nibble, q_v in the high one.
+    __device__ static float m(const Raw& r, int j, float tm, float) {
+        const unsigned w = j < 4 ? r.w.x : r.w.y;
+        return __shfl_sync(0xffffffffu, tm, (int)(w >> (8 * (j & 3))), 16);
+    }
+    __device__ static float v(const Raw& r, int j, float tv) {
+        const unsigned w = j < 4 ? r.w.x : r.w.y;
+        return __shfl_sync(0xffffffffu, tv, (int)(w >> (8 * (j & 3) + 4)), 16);
+    }
+};
+template <> struct TableCodes<MDQ_LAYOUT_M8V4> {
+    struct Raw { uint2 w; unsigned vw; };
+    __device__ static void load8(const TensorPtrs& t, int64_t e, Raw& r) {
+        r.w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const int8_t*>(t.m) + e));
+        r.vw = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(t.v) + (e >> 1)));
+    }
+    // int8 m codes have 256 values: converted directly.
+    __device__ static float m(const Raw& r, int j, float, float sm) {
+        const unsigned w = j < 4 ? r.w.x : r.w.y;
+        const int q = (int)(int8_t)(uint8_t)(w >> (8 * (j & 3)));
+        return __fmul_rn(small_int_to_float(q), sm);
+    }
+    __device__ static float v(const Raw& r, int j, float tv) {
+        return __shfl_sync(0xffffffffu, tv, (int)(r.vw >> (4 * j)), 16);
+    }
+};
+template <int LAYOUT> struct TableCodes { struct Raw {}; };
+
 // One tile of 2048 elements.  FULL: every thread owns 8 in-range elements and
 // all pointers allow vector access; otherwise element-wise guarded access.
 // `red` is this tile's reduction scratch.
-template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL, int PT>
+template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL, int PT, bool TBL>
 __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                                           float4* red,
                                           unsigned long long (&pc)[kProfSlots],
@@ -187,8 +231,12 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     }
 
     // ---- load ----------------------------------------------------------
+    // TBL: 4-bit codes dequantised by table (full tiles only).
+    constexpr bool kTab = TBL && FULL;
+    using TC = TableCodes<LAYOUT>;
     float p[PT], g[PT];
     int qm[PT], qv[PT];
+    typename TC::Raw raw[PT / 8];
     if (FULL) {
 #pragma unroll
         for (int h = 0; h < PT / 8; ++h) {
@@ -197,14 +245,19 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
             p[8 * h + 0] = a.x; p[8 * h + 1] = a.y; p[8 * h + 2] = a.z; p[8 * h + 3] = a.w;
             p[8 * h + 4] = b.x; p[8 * h + 5] = b.y; p[8 * h + 6] = b.z; p[8 * h + 7] = b.w;
             float gg[8];
-            int am[8], av[8];
             Grad<GT>::load8(T.g, e0 + 8 * h, gg);
-            CI::load8(T, e0 + 8 * h, am, av);
 #pragma unroll
-            for (int j = 0; j < PT; ++j) {
-                g[8 * h + j] = gg[j];
-                qm[8 * h + j] = am[j];
-                qv[8 * h + j] = av[j];
+            for (int j = 0; j < 8; ++j) g[8 * h + j] = gg[j];
+            if constexpr (kTab) {
+                TC::load8(T, e0 + 8 * h, raw[h]);
+            } else {
+                int am[8], av[8];
+                CI::load8(T, e0 + 8 * h, am, av);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    qm[8 * h + j] = am[j];
+                    qv[8 * h + j] = av[j];
+                }
             }
         }
     } else {
@@ -224,12 +277,26 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     // ---- dequantise, AdamW moments, parameter update -------------------
     // (CUDA/stquant_kernel.cu:163-177, 220-229)
     float m[PT], v[PT];
+    if constexpr (kTab) {
+        const float kf = small_int_to_float(tid & 15);
+        const float tv = dequant_v(kf, sv, vmn);
+        const float tm = __fmul_rn(__fsub_rn(kf, 8.0f), sm);
 #pragma unroll
-    for (int j = 0; j < PT; ++j) {
-        const float qmf = kMagicC ? small_int_to_float(qm[j]) : (float)qm[j];
-        m[j] = __fmul_rn(qmf, sm);
-        const float qvf = kMagicC ? small_int_to_float(qv[j]) : (float)(unsigned)qv[j];
-        v[j] = dequant_v(qvf, sv, vmn);
+        for (int h = 0; h < PT / 8; ++h) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                m[8 * h + j] = TC::m(raw[h], j, tm, sm);
+                v[8 * h + j] = TC::v(raw[h], j, tv);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < PT; ++j) {
+            const float qmf = kMagicC ? small_int_to_float(qm[j]) : (float)qm[j];
+            m[j] = __fmul_rn(qmf, sm);
+            const float qvf = kMagicC ? small_int_to_float(qv[j]) : (float)(unsigned)qv[j];
+            v[j] = dequant_v(qvf, sv, vmn);
+        }
     }
     if (PROF && tid == 0) prof_mark(pc, 0, t0);
 #pragma unroll
@@ -268,8 +335,11 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     for (int j = 0; j < PT; ++j) {
         const bool ok = FULL || j < cnt;
         st[0] = fmaxf(st[0], ok ? fabsf(m[j]) : 0.0f);
-        st[1] = fmaxf(st[1], x[j]);
-        st[2] = fminf(st[2], x[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < PT; j += 2) {
+        st[1] = max3f(st[1], x[j], x[j + 1]);
+        st[2] = min3f(st[2], x[j], x[j + 1]);
     }
     group_reduce<0b011u>(st, gthreads, red);
     const float lmax = logf(st[1]);
@@ -358,7 +428,7 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
 // CTA-wide barriers happen only at a tensor switch and, for blocks spanning
 // several warps, inside the block reduction.
 // ---------------------------------------------------------------------------
-template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT>
+template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT, bool TBL>
 __global__ void __launch_bounds__(threads_for<PT>(), PT == 8 ? MDQ_MIN_CTAS_PER_SM : MDQ_MIN_CTAS_PT16)
 mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
     constexpr int kTileT = kTile;
@@ -398,9 +468,9 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
 
         float4* red = s_red[tile & 1];
         if (s_ctx.vec && tile_e0 + kTileT <= n)
-            tile_body<LAYOUT, GT, EXACT_P, PROF, true, PT>(s_ctx, tile_e0, red, pc, t0);
+            tile_body<LAYOUT, GT, EXACT_P, PROF, true, PT, TBL>(s_ctx, tile_e0, red, pc, t0);
         else
-            tile_body<LAYOUT, GT, EXACT_P, PROF, false, PT>(s_ctx, tile_e0, red, pc, t0);
+            tile_body<LAYOUT, GT, EXACT_P, PROF, false, PT, TBL>(s_ctx, tile_e0, red, pc, t0);
     }
     if (PROF && tid == 0 && P.prof != nullptr) {
         for (int k = 0; k < kProfSlots; ++k) atomicAdd(P.prof + k, pc[k]);
@@ -654,9 +724,9 @@ int blocks_per_sm(K kernel, int threads) {
     return b;
 }
 
-template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT>
+template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT, bool TBL>
 mdq_status launch_tiles_t(const mdq::LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
-    auto k = mdq::mdq_step_tiles<LAYOUT, GT, EXACT_P, PROF, CAP, PT>;
+    auto k = mdq::mdq_step_tiles<LAYOUT, GT, EXACT_P, PROF, CAP, PT, TBL>;
     static int occ = 0;  // per instantiation; identical across B200 devices
     constexpr int kNT = mdq::threads_for<PT>();
     if (occ == 0) occ = blocks_per_sm(k, kNT);
@@ -668,44 +738,52 @@ mdq_status launch_tiles_t(const mdq::LaunchParams<CAP>& P, int sms, cudaStream_t
     return MDQ_OK;
 }
 
-template <int LAYOUT, typename GT, int CAP, int PT>
+template <int LAYOUT, typename GT, int CAP, int PT, bool TBL>
 mdq_status launch_tiles_pt(const mdq::LaunchParams<CAP>& P, bool exact, bool prof, int sms,
                            cudaStream_t s) {
     if (exact) {
-        return prof ? launch_tiles_t<LAYOUT, GT, true, true, CAP, PT>(P, sms, s)
-                    : launch_tiles_t<LAYOUT, GT, true, false, CAP, PT>(P, sms, s);
+        return prof ? launch_tiles_t<LAYOUT, GT, true, true, CAP, PT, TBL>(P, sms, s)
+                    : launch_tiles_t<LAYOUT, GT, true, false, CAP, PT, TBL>(P, sms, s);
     }
-    return prof ? launch_tiles_t<LAYOUT, GT, false, true, CAP, PT>(P, sms, s)
-                : launch_tiles_t<LAYOUT, GT, false, false, CAP, PT>(P, sms, s);
+    return prof ? launch_tiles_t<LAYOUT, GT, false, true, CAP, PT, TBL>(P, sms, s)
+                : launch_tiles_t<LAYOUT, GT, false, false, CAP, PT, TBL>(P, sms, s);
 }
 
+// Table dequantisation for 4-bit v codes when every 16-lane half-warp lies in
+// one block (block >= 16 * PT).
 template <int LAYOUT, typename GT, int CAP>
 mdq_status launch_tiles_mode(const mdq::LaunchParams<CAP>& P, bool exact, bool prof, int sms,
-                             int pt, cudaStream_t s) {
-    return pt == 16 ? launch_tiles_pt<LAYOUT, GT, CAP, 16>(P, exact, prof, sms, s)
-                    : launch_tiles_pt<LAYOUT, GT, CAP, 8>(P, exact, prof, sms, s);
+                             int pt, int min_block, cudaStream_t s) {
+    constexpr bool kV4 = LAYOUT == MDQ_LAYOUT_PACKED4 || LAYOUT == MDQ_LAYOUT_M8V4;
+    if constexpr (kV4) {
+        // (4-bit v layouts run PT = 16 whenever the block allows tables.)
+        if (MDQ_USE_TABLES && pt == 16 && min_block >= 16 * pt)
+            return launch_tiles_pt<LAYOUT, GT, CAP, 16, true>(P, exact, prof, sms, s);
+    }
+    return pt == 16 ? launch_tiles_pt<LAYOUT, GT, CAP, 16, false>(P, exact, prof, sms, s)
+                    : launch_tiles_pt<LAYOUT, GT, CAP, 8, false>(P, exact, prof, sms, s);
 }
 
 template <int CAP>
 mdq_status launch_tiles(int layout, int gdt, const mdq::LaunchParams<CAP>& P, bool exact, bool prof,
-                        int sms, int pt, cudaStream_t s) {
+                        int sms, int pt, int min_block, cudaStream_t s) {
     const bool bf = gdt == MDQ_BF16;
     switch (layout) {
         case MDQ_LAYOUT_PACKED4:
-            return bf ? launch_tiles_mode<MDQ_LAYOUT_PACKED4, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, s)
-                      : launch_tiles_mode<MDQ_LAYOUT_PACKED4, float, CAP>(P, exact, prof, sms, pt, s);
+            return bf ? launch_tiles_mode<MDQ_LAYOUT_PACKED4, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, min_block, s)
+                      : launch_tiles_mode<MDQ_LAYOUT_PACKED4, float, CAP>(P, exact, prof, sms, pt, min_block, s);
         case MDQ_LAYOUT_S8U8:
-            return bf ? launch_tiles_mode<MDQ_LAYOUT_S8U8, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, s)
-                      : launch_tiles_mode<MDQ_LAYOUT_S8U8, float, CAP>(P, exact, prof, sms, pt, s);
+            return bf ? launch_tiles_mode<MDQ_LAYOUT_S8U8, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, min_block, s)
+                      : launch_tiles_mode<MDQ_LAYOUT_S8U8, float, CAP>(P, exact, prof, sms, pt, min_block, s);
         case MDQ_LAYOUT_S16U16:
-            return bf ? launch_tiles_mode<MDQ_LAYOUT_S16U16, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, s)
-                      : launch_tiles_mode<MDQ_LAYOUT_S16U16, float, CAP>(P, exact, prof, sms, pt, s);
+            return bf ? launch_tiles_mode<MDQ_LAYOUT_S16U16, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, min_block, s)
+                      : launch_tiles_mode<MDQ_LAYOUT_S16U16, float, CAP>(P, exact, prof, sms, pt, min_block, s);
         case MDQ_LAYOUT_S32U32:
-            return bf ? launch_tiles_mode<MDQ_LAYOUT_S32U32, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, s)
-                      : launch_tiles_mode<MDQ_LAYOUT_S32U32, float, CAP>(P, exact, prof, sms, pt, s);
+            return bf ? launch_tiles_mode<MDQ_LAYOUT_S32U32, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, min_block, s)
+                      : launch_tiles_mode<MDQ_LAYOUT_S32U32, float, CAP>(P, exact, prof, sms, pt, min_block, s);
         case MDQ_LAYOUT_M8V4:
-            return bf ? launch_tiles_mode<MDQ_LAYOUT_M8V4, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, s)
-                      : launch_tiles_mode<MDQ_LAYOUT_M8V4, float, CAP>(P, exact, prof, sms, pt, s);
+            return bf ? launch_tiles_mode<MDQ_LAYOUT_M8V4, __nv_bfloat16, CAP>(P, exact, prof, sms, pt, min_block, s)
+                      : launch_tiles_mode<MDQ_LAYOUT_M8V4, float, CAP>(P, exact, prof, sms, pt, min_block, s);
     }
     return fail(MDQ_ERR_INVALID_ARG, "bad layout %d", layout);
 }
@@ -783,7 +861,7 @@ mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bo
         P.total_tiles = (int32_t)tiles;
         const mdq_tensor_desc& d0 = descs[idx[i - 1]];
         const mdq_status st = launch_tiles<CAP>(d0.layout, d0.grad_dtype, P, exact, prof != nullptr,
-                                                sms, pt, s);
+                                                sms, pt, min_block, s);
         if (st != MDQ_OK) return st;
     }
     return MDQ_OK;

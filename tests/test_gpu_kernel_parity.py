@@ -136,10 +136,11 @@ def test_many_tensors_one_launch(ref, cuda_device):
         assert all(v == 0 for v in mm.values()), mm
 
 
-def test_mixed_m8_v4_codes(ref, cuda_device):
+@pytest.mark.parametrize("block", [128, 256, 1024])
+def test_mixed_m8_v4_codes(ref, cuda_device, block):
     """8-bit m + 4-bit v: m codes equal an all-8-bit reference run's, v codes an
     all-4-bit run's (m and v never depend on each other in the step)."""
-    n, block = 100_000, 256
+    n = 100_000
     r8 = State(n, block, "s8u8", cuda_device, seed=5)
     r4 = State(n, block, "packed4", cuda_device, seed=5)
     mine_m = torch.zeros(n, dtype=torch.int8, device=cuda_device)
@@ -216,8 +217,9 @@ def adversarial_grad(kind, n, step, device):
 
 
 @pytest.mark.parametrize("kind", ADVERSARIAL)
-@pytest.mark.parametrize("layout,bits,block", [("packed4", 4, 128), ("s8u8", 8, 1024),
-                                                ("s8u8", 8, 64), ("s16u16", 16, 256)])
+@pytest.mark.parametrize("layout,bits,block", [("packed4", 4, 128), ("packed4", 4, 1024),
+                                                ("s8u8", 8, 1024), ("s8u8", 8, 64),
+                                                ("s16u16", 16, 256)])
 def test_adversarial_inputs_bit_exact(ref, cuda_device, kind, layout, bits, block):
     """Degenerate and non-finite gradients: still bit-identical to the reference
     (NaN compared by bit pattern)."""
