@@ -30,12 +30,11 @@ __device__ __forceinline__ unsigned pack_low_bytes(unsigned a, unsigned b, unsig
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// Magic word of (16 * qhi + qlo + bias) from the magic words of qhi and qlo,
-// in float arithmetic (exact: every intermediate is an integer below 2^22
-// offset by the magic constant).  Its low byte is the packed nibble pair.
-__device__ __forceinline__ unsigned nibble_pair(int hi_word, int lo_word, float bias) {
-    const float rhi = __fsub_rn(__int_as_float(hi_word), kMagic);
-    return (unsigned)__float_as_int(__fmaf_rn(rhi, 16.0f, __fadd_rn(__int_as_float(lo_word), bias)));
+// 16 * hi_word + lo_word in one integer multiply-add: since 17 * 0x4B400000
+// has a zero low byte, its low byte is 16 * qhi + qlo (mod 256) for the codes
+// qhi, qlo of two magic words: the packed nibble pair when both are in [0, 15].
+__device__ __forceinline__ unsigned nibble_pair(int hi_word, int lo_word) {
+    return (unsigned)hi_word * 16u + (unsigned)lo_word;
 }
 
 // Exact float of a small integer (|q| < 2^22) without an I2F instruction.
@@ -61,6 +60,9 @@ template <int LAYOUT> struct Codes;
 template <> struct Codes<MDQ_LAYOUT_PACKED4> {
     static constexpr bool kApproxLog = true;
     static constexpr bool kMagicCodes = true;
+    // m words carry the nibble bias: kMagicBits + q_m + 8 (rounding adds
+    // 1.5 * 2^23 + 8), so the word's low nibble is the stored nibble.
+    static constexpr int kMBias = 8;
     __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
         const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(t.m) + e));
 #pragma unroll
@@ -79,14 +81,14 @@ template <> struct Codes<MDQ_LAYOUT_PACKED4> {
     // (m_bits, v_bits <= 4), so the reference's nibble clamps
     // (CUDA/stquant_kernel.cu:120-128) never bind and masking suffices.
     __device__ static unsigned byte_of(int mw, int vw) {
-        return (((unsigned)vw & 15u) << 4) | (((unsigned)mw + 8u) & 15u);
+        return (((unsigned)vw & 15u) << 4) | ((unsigned)mw & 15u);
     }
-    // Byte = 16 q_v + (q_m + 8), formed in float arithmetic and gathered with
-    // byte permutes (magic words keep every value exact).
+    // Byte = 16 q_v + (q_m + 8), one multiply-add of the two words, gathered
+    // with byte permutes.
     __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
         unsigned b[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) b[j] = nibble_pair(vw[j], mw[j], 8.0f);
+        for (int j = 0; j < 8; ++j) b[j] = nibble_pair(vw[j], mw[j]);
         __stcs(reinterpret_cast<uint2*>(static_cast<uint8_t*>(t.m) + e),
                make_uint2(pack_low_bytes(b[0], b[1], b[2], b[3]), pack_low_bytes(b[4], b[5], b[6], b[7])));
     }
@@ -96,12 +98,13 @@ template <> struct Codes<MDQ_LAYOUT_PACKED4> {
     // (int)q as CUDA/stquant_kernel.cu:118,126, as a magic word.  A NaN code
     // (NaN or infinite gradients) leaves the reference build's nibble at 0,
     // i.e. q = -8: its integer conversion of NaN lands below the nibble clamp.
-    __device__ static int m_word(double q) { return kMagicBits + (isnan(q) ? -8 : (int)q); }
+    __device__ static int m_word(double q) { return kMagicBits + kMBias + (isnan(q) ? -8 : (int)q); }
     __device__ static int v_word(double q) { return kMagicBits + (int)q; }
 };
 
 template <typename MT, typename VT, bool MAGIC> struct CodesPlain {
     static constexpr bool kMagicCodes = MAGIC;
+    static constexpr int kMBias = 0;
     template <typename T>
     __device__ static void ld8(const T* src, int (&o)[8]) {
         if constexpr (sizeof(T) == 1) {
@@ -180,6 +183,7 @@ template <> struct Codes<MDQ_LAYOUT_S32U32> : CodesPlain<int32_t, uint32_t, fals
 template <> struct Codes<MDQ_LAYOUT_M8V4> {
     static constexpr bool kApproxLog = true;
     static constexpr bool kMagicCodes = true;
+    static constexpr int kMBias = 0;
     __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
         const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const int8_t*>(t.m) + e));
         const unsigned vw = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(t.v) + (e >> 1)));
@@ -198,8 +202,8 @@ template <> struct Codes<MDQ_LAYOUT_M8V4> {
         const unsigned lo = pack_low_bytes(mw[0], mw[1], mw[2], mw[3]);
         const unsigned hi = pack_low_bytes(mw[4], mw[5], mw[6], mw[7]);
         // v codes are within [0, 15] (4-bit levels), so pairs pack exactly.
-        const unsigned nib = pack_low_bytes(nibble_pair(vw[1], vw[0], 0.0f), nibble_pair(vw[3], vw[2], 0.0f),
-                                            nibble_pair(vw[5], vw[4], 0.0f), nibble_pair(vw[7], vw[6], 0.0f));
+        const unsigned nib = pack_low_bytes(nibble_pair(vw[1], vw[0]), nibble_pair(vw[3], vw[2]),
+                                            nibble_pair(vw[5], vw[4]), nibble_pair(vw[7], vw[6]));
         __stcs(reinterpret_cast<uint2*>(static_cast<int8_t*>(t.m) + e), make_uint2(lo, hi));
         __stcs(reinterpret_cast<unsigned*>(static_cast<uint8_t*>(t.v) + (e >> 1)), nib);
     }

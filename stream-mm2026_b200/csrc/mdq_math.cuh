@@ -178,10 +178,13 @@ __device__ __forceinline__ float max_nan(float a, float b) {
     return r;
 }
 
-template <bool CORRECT>
+// BIAS (0..255) is added to the word: the magic constant 1.5 * 2^23 + BIAS
+// rounds the same way (floats in [2^23, 2^24) are the integers).
+template <bool CORRECT, int BIAS = 0>
 __device__ __forceinline__ int round_checked(float y, float x, float d, float half_d, float& rem) {
-    float s = __fadd_rn(y, 12582912.0f);
-    float r = __fsub_rn(s, 12582912.0f);
+    constexpr float kM = 12582912.0f + (float)BIAS;
+    float s = __fadd_rn(y, kM);
+    float r = __fsub_rn(s, kM);
     float e = __fmaf_rn(-r, d, x);
     if (CORRECT) {
         const float stp = e >= half_d ? 1.0f : (e <= -half_d ? -1.0f : 0.0f);

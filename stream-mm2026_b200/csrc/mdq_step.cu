@@ -59,6 +59,9 @@ constexpr int kProfSlots = 5;
 #ifndef MDQ_MIN_CTAS_PT16
 #define MDQ_MIN_CTAS_PT16 4
 #endif
+#ifndef MDQ_GROUP_BARRIER
+#define MDQ_GROUP_BARRIER 1
+#endif
 #ifndef MDQ_USE_TABLES
 #define MDQ_USE_TABLES 1
 #endif
@@ -144,7 +147,12 @@ __device__ __forceinline__ void group_reduce(float (&x)[NV], int gthreads, float
             v.w = NV > 3 ? x[3 % NV] : 0.0f;
             red[w] = v;
         }
-        __syncthreads();
+        // Only the warps of one block exchange partials: they meet at their
+        // own named barrier (ids 1..), so other blocks' warps run on.
+        if (MDQ_GROUP_BARRIER && gthreads < (int)blockDim.x)
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + w / (gthreads >> 5)), "r"(gthreads) : "memory");
+        else
+            __syncthreads();
         const int wpg = gthreads >> 5;
         const int w0 = (w / wpg) * wpg;
         for (int i = 0; i < wpg; ++i) {
@@ -377,47 +385,56 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     // accepted code already lies in its level range (|m| <= max|m| bounds
     // m / dm by L (1 + 2^-22); accepted v codes have |X'/dv - r| < 1/2 with
     // X' in [-errx, lmax - lmin + errx]).
-    const int mw_hi = kMagicBits + (int)C.lm_f - 1;
-    int mw[PT], vw[PT];
-    float rem_m = 0.0f, rem_v = 0.0f;
+    constexpr int kB = CI::kMBias;
+    const int mw_hi = kMagicBits + kB + (int)C.lm_f - 1;
+    // Codes of all PT elements are formed and checked, then stored (forming
+    // and storing them eight at a time measured slower).
+    constexpr int G = PT;
 #pragma unroll
-    for (int j = 0; j < PT; ++j) {
-        float r;
-        mw[j] = min(round_checked<kCorrect>(__fmul_rn(m[j], rdm), m[j], dm, half_dm, r), mw_hi);
-        rem_m = max_nan(rem_m, r);
-        const float xv = kApprox ? __fmaf_rn(approx_log2(x[j]), kLn2, -lmin)
-                                 : __fsub_rn(logf(x[j]), lmin);
-        vw[j] = round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
-        rem_v = max_nan(rem_v, r);
-    }
-    if (!kMagicC || !(rem_m < half_dm && rem_v < thr_v)) {
-        // Rare: codes that fail their check take the reference's
-        // double-precision expression (all of them for 32-bit codes).
+    for (int h0 = 0; h0 < PT; h0 += G) {
+        int mw[G], vw[G];
+        float rem_m = 0.0f, rem_v = 0.0f;
 #pragma unroll
-        for (int j = 0; j < PT; ++j) {
+        for (int j = 0; j < G; ++j) {
+            const int k = h0 + j;
             float r;
-            round_checked<kCorrect>(__fmul_rn(m[j], rdm), m[j], dm, half_dm, r);
-            if (!kMagicC || !(r < half_dm)) mw[j] = CI::m_word(requant_m_ref(m[j], dm, C.lm_d));
-            const float xv = kApprox ? __fmaf_rn(approx_log2(x[j]), kLn2, -lmin)
-                                 : __fsub_rn(logf(x[j]), lmin);
-            round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
-            if (!kMagicC || !(r < thr_v))
-                vw[j] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[j]), lmin), dv, C.lv_d));
+            mw[j] = min(round_checked<kCorrect, kB>(__fmul_rn(m[k], rdm), m[k], dm, half_dm, r), mw_hi);
+            rem_m = max_nan(rem_m, r);
+            const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -lmin)
+                                     : __fsub_rn(logf(x[k]), lmin);
+            vw[j] = round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
+            rem_v = max_nan(rem_v, r);
         }
-    }
-    if (FULL) {
+        if (!kMagicC || !(rem_m < half_dm && rem_v < thr_v)) {
+            // Rare: codes that fail their check take the reference's
+            // double-precision expression (all of them for 32-bit codes).
 #pragma unroll
-        for (int h = 0; h < PT / 8; ++h) {
-            int a[8], b[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) { a[j] = mw[8 * h + j]; b[j] = vw[8 * h + j]; }
-            CI::store8(T, e0 + 8 * h, a, b);
+            for (int j = 0; j < G; ++j) {
+                const int k = h0 + j;
+                float r;
+                round_checked<kCorrect>(__fmul_rn(m[k], rdm), m[k], dm, half_dm, r);
+                if (!kMagicC || !(r < half_dm)) mw[j] = CI::m_word(requant_m_ref(m[k], dm, C.lm_d));
+                const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -lmin)
+                                         : __fsub_rn(logf(x[k]), lmin);
+                round_checked<kCorrect>(__fmul_rn(xv, rdv), xv, dv, half_dv, r);
+                if (!kMagicC || !(r < thr_v))
+                    vw[j] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[k]), lmin), dv, C.lv_d));
+            }
         }
-    } else {
-        // One thread owns all its elements, so M8V4 nibble pairs never race.
+        if (FULL) {
 #pragma unroll
-        for (int j = 0; j < PT; ++j)
-            if (j < cnt) CI::store1(T, e0 + j, mw[j], vw[j]);
+            for (int h = 0; h < G / 8; ++h) {
+                int a[8], b[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) { a[j] = mw[8 * h + j]; b[j] = vw[8 * h + j]; }
+                CI::store8(T, e0 + h0 + 8 * h, a, b);
+            }
+        } else {
+            // One thread owns all its elements, so M8V4 nibble pairs never race.
+#pragma unroll
+            for (int j = 0; j < G; ++j)
+                if (h0 + j < cnt) CI::store1(T, e0 + h0 + j, mw[j], vw[j]);
+        }
     }
     if (PROF && tid == 0) prof_mark(pc, 3, t0);
 }
