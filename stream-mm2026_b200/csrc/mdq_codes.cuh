@@ -1,9 +1,9 @@
 // mdq_codes.cuh - moment-code storage layouts and gradient loads.
 //
-// Every layout exposes the same per-thread interface over 8 consecutive
+// Every layout exposes the same per-thread interface over 4 consecutive
 // elements (vectorised) or one element (scalar):
-//   load8 / load1   -> signed m code values, unsigned v code values
-//   store8 / store1 <- codes as "magic" words (see below)
+//   load4 / load1   -> signed m code values, unsigned v code values
+//   store4 / store1 <- codes as "magic" words (see below)
 //   m_word / v_word    the reference's integer conversion of a code computed on
 //                      the double path, as a magic word
 //
@@ -63,11 +63,11 @@ template <> struct Codes<MDQ_LAYOUT_PACKED4> {
     // m words carry the nibble bias: kMagicBits + q_m + 8 (rounding adds
     // 1.5 * 2^23 + 8), so the word's low nibble is the stored nibble.
     static constexpr int kMBias = 8;
-    __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
-        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(t.m) + e));
+    __device__ static void load4(const TensorPtrs& t, int64_t e, int (&qm)[4], int (&qv)[4]) {
+        const unsigned w = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(t.m) + e));
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const unsigned b = (j < 4 ? w.x : w.y) >> (8 * (j & 3));
+        for (int j = 0; j < 4; ++j) {
+            const unsigned b = w >> (8 * j);
             qm[j] = (int)(b & 15u) - 8;
             qv[j] = (int)((b >> 4) & 15u);
         }
@@ -85,12 +85,10 @@ template <> struct Codes<MDQ_LAYOUT_PACKED4> {
     }
     // Byte = 16 q_v + (q_m + 8), one multiply-add of the two words, gathered
     // with byte permutes.
-    __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
-        unsigned b[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) b[j] = nibble_pair(vw[j], mw[j]);
-        __stcs(reinterpret_cast<uint2*>(static_cast<uint8_t*>(t.m) + e),
-               make_uint2(pack_low_bytes(b[0], b[1], b[2], b[3]), pack_low_bytes(b[4], b[5], b[6], b[7])));
+    __device__ static void store4(const TensorPtrs& t, int64_t e, const int (&mw)[4], const int (&vw)[4]) {
+        __stcs(reinterpret_cast<unsigned*>(static_cast<uint8_t*>(t.m) + e),
+               pack_low_bytes(nibble_pair(vw[0], mw[0]), nibble_pair(vw[1], mw[1]),
+                              nibble_pair(vw[2], mw[2]), nibble_pair(vw[3], mw[3])));
     }
     __device__ static void store1(const TensorPtrs& t, int64_t e, int mw, int vw) {
         static_cast<uint8_t*>(t.m)[e] = (uint8_t)byte_of(mw, vw);
@@ -106,57 +104,47 @@ template <typename MT, typename VT, bool MAGIC> struct CodesPlain {
     static constexpr bool kMagicCodes = MAGIC;
     static constexpr int kMBias = 0;
     template <typename T>
-    __device__ static void ld8(const T* src, int (&o)[8]) {
+    __device__ static void ld4(const T* src, int (&o)[4]) {
         if constexpr (sizeof(T) == 1) {
+            const unsigned w = __ldcs(reinterpret_cast<const unsigned*>(src));
+            const T* b = reinterpret_cast<const T*>(&w);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = (int)b[j];
+        } else if constexpr (sizeof(T) == 2) {
             const uint2 w = __ldcs(reinterpret_cast<const uint2*>(src));
             const T* b = reinterpret_cast<const T*>(&w);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = (int)b[j];
-        } else if constexpr (sizeof(T) == 2) {
+            for (int j = 0; j < 4; ++j) o[j] = (int)b[j];
+        } else {
             const uint4 w = __ldcs(reinterpret_cast<const uint4*>(src));
             const T* b = reinterpret_cast<const T*>(&w);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = (int)b[j];
-        } else {
-            const uint4 w0 = __ldcs(reinterpret_cast<const uint4*>(src));
-            const uint4 w1 = __ldcs(reinterpret_cast<const uint4*>(src) + 1);
-            const T* b0 = reinterpret_cast<const T*>(&w0);
-            const T* b1 = reinterpret_cast<const T*>(&w1);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) { o[j] = (int)b0[j]; o[j + 4] = (int)b1[j]; }
+            for (int j = 0; j < 4; ++j) o[j] = (int)b[j];
         }
     }
     template <typename T>
-    __device__ static void st8(T* dst, const int (&o)[8]) {
+    __device__ static void st4(T* dst, const int (&o)[4]) {
         if constexpr (sizeof(T) == 1) {
-            const unsigned lo = pack_low_bytes(o[0], o[1], o[2], o[3]);
-            const unsigned hi = pack_low_bytes(o[4], o[5], o[6], o[7]);
-            __stcs(reinterpret_cast<uint2*>(dst), make_uint2(lo, hi));
+            __stcs(reinterpret_cast<unsigned*>(dst), pack_low_bytes(o[0], o[1], o[2], o[3]));
         } else if constexpr (sizeof(T) == 2) {
-            uint4 w;
-            w.x = ((unsigned)o[0] & 0xffffu) | ((unsigned)o[1] << 16);
-            w.y = ((unsigned)o[2] & 0xffffu) | ((unsigned)o[3] << 16);
-            w.z = ((unsigned)o[4] & 0xffffu) | ((unsigned)o[5] << 16);
-            w.w = ((unsigned)o[6] & 0xffffu) | ((unsigned)o[7] << 16);
-            __stcs(reinterpret_cast<uint4*>(dst), w);
+            __stcs(reinterpret_cast<uint2*>(dst),
+                   make_uint2(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410)));
         } else {
             __stcs(reinterpret_cast<uint4*>(dst),
                    make_uint4((unsigned)o[0], (unsigned)o[1], (unsigned)o[2], (unsigned)o[3]));
-            __stcs(reinterpret_cast<uint4*>(dst) + 1,
-                   make_uint4((unsigned)o[4], (unsigned)o[5], (unsigned)o[6], (unsigned)o[7]));
         }
     }
-    __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
-        ld8(static_cast<const MT*>(t.m) + e, qm);
-        ld8(static_cast<const VT*>(t.v) + e, qv);
+    __device__ static void load4(const TensorPtrs& t, int64_t e, int (&qm)[4], int (&qv)[4]) {
+        ld4(static_cast<const MT*>(t.m) + e, qm);
+        ld4(static_cast<const VT*>(t.v) + e, qv);
     }
     __device__ static void load1(const TensorPtrs& t, int64_t e, int& qm, int& qv) {
         qm = (int)static_cast<const MT*>(t.m)[e];
         qv = (int)static_cast<const VT*>(t.v)[e];
     }
-    __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
-        st8(static_cast<MT*>(t.m) + e, mw);
-        st8(static_cast<VT*>(t.v) + e, vw);
+    __device__ static void store4(const TensorPtrs& t, int64_t e, const int (&mw)[4], const int (&vw)[4]) {
+        st4(static_cast<MT*>(t.m) + e, mw);
+        st4(static_cast<VT*>(t.v) + e, vw);
     }
     // Magic words and plain integers both truncate to the stored code.
     __device__ static void store1(const TensorPtrs& t, int64_t e, int mw, int vw) {
@@ -184,13 +172,12 @@ template <> struct Codes<MDQ_LAYOUT_M8V4> {
     static constexpr bool kApproxLog = true;
     static constexpr bool kMagicCodes = true;
     static constexpr int kMBias = 0;
-    __device__ static void load8(const TensorPtrs& t, int64_t e, int (&qm)[8], int (&qv)[8]) {
-        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const int8_t*>(t.m) + e));
-        const unsigned vw = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(t.v) + (e >> 1)));
-        const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+    __device__ static void load4(const TensorPtrs& t, int64_t e, int (&qm)[4], int (&qv)[4]) {
+        const unsigned w = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const int8_t*>(t.m) + e));
+        const unsigned vw = __ldcs(reinterpret_cast<const unsigned short*>(static_cast<const uint8_t*>(t.v) + (e >> 1)));
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            qm[j] = b[j];
+        for (int j = 0; j < 4; ++j) {
+            qm[j] = (int)(int8_t)(uint8_t)(w >> (8 * j));
             qv[j] = (int)((vw >> (4 * j)) & 15u);
         }
     }
@@ -198,14 +185,12 @@ template <> struct Codes<MDQ_LAYOUT_M8V4> {
         qm = static_cast<const int8_t*>(t.m)[e];
         qv = (int)((static_cast<const uint8_t*>(t.v)[e >> 1] >> (4 * (e & 1))) & 15u);
     }
-    __device__ static void store8(const TensorPtrs& t, int64_t e, const int (&mw)[8], const int (&vw)[8]) {
-        const unsigned lo = pack_low_bytes(mw[0], mw[1], mw[2], mw[3]);
-        const unsigned hi = pack_low_bytes(mw[4], mw[5], mw[6], mw[7]);
+    __device__ static void store4(const TensorPtrs& t, int64_t e, const int (&mw)[4], const int (&vw)[4]) {
+        __stcs(reinterpret_cast<unsigned*>(static_cast<int8_t*>(t.m) + e),
+               pack_low_bytes(mw[0], mw[1], mw[2], mw[3]));
         // v codes are within [0, 15] (4-bit levels), so pairs pack exactly.
-        const unsigned nib = pack_low_bytes(nibble_pair(vw[1], vw[0]), nibble_pair(vw[3], vw[2]),
-                                            nibble_pair(vw[5], vw[4]), nibble_pair(vw[7], vw[6]));
-        __stcs(reinterpret_cast<uint2*>(static_cast<int8_t*>(t.m) + e), make_uint2(lo, hi));
-        __stcs(reinterpret_cast<unsigned*>(static_cast<uint8_t*>(t.v) + (e >> 1)), nib);
+        const unsigned nib = __byte_perm(nibble_pair(vw[1], vw[0]), nibble_pair(vw[3], vw[2]), 0x0040);
+        __stcs(reinterpret_cast<unsigned short*>(static_cast<uint8_t*>(t.v) + (e >> 1)), (unsigned short)nib);
     }
     // Neighbouring elements share a byte: callers give each byte one owner.
     __device__ static void store1(const TensorPtrs& t, int64_t e, int mw, int vw) {
@@ -226,23 +211,19 @@ template <> struct Codes<MDQ_LAYOUT_M8V4> {
 // Gradient loads (fp32, or bf16 widened exactly).
 template <typename GT> struct Grad;
 template <> struct Grad<float> {
-    __device__ static void load8(const void* g, int64_t e, float (&o)[8]) {
-        const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(g) + e);
-        const float4 a = __ldcs(s), b = __ldcs(s + 1);
+    __device__ static void load4(const void* g, int64_t e, float (&o)[4]) {
+        const float4 a = __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(g) + e));
         o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
-        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
     }
     __device__ static float load1(const void* g, int64_t e) { return static_cast<const float*>(g)[e]; }
 };
 template <> struct Grad<__nv_bfloat16> {
-    __device__ static void load8(const void* g, int64_t e, float (&o)[8]) {
-        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(g) + e));
-        const unsigned u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            o[2 * j] = __uint_as_float(u[j] << 16);
-            o[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
-        }
+    __device__ static void load4(const void* g, int64_t e, float (&o)[4]) {
+        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(g) + e));
+        o[0] = __uint_as_float(w.x << 16);
+        o[1] = __uint_as_float(w.x & 0xffff0000u);
+        o[2] = __uint_as_float(w.y << 16);
+        o[3] = __uint_as_float(w.y & 0xffff0000u);
     }
     __device__ static float load1(const void* g, int64_t e) {
         return __bfloat162float(static_cast<const __nv_bfloat16*>(g)[e]);

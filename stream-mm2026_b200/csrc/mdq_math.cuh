@@ -123,7 +123,7 @@ __device__ __forceinline__ float scale_v_of(float max_lv, float min_lv, const St
 // ---------------------------------------------------------------------------
 
 // Reference expression for a signed (m) code, clamped to [-L, L-1].
-__device__ __noinline__ double requant_m_ref(float x, float d, double lm) {
+static __device__ __noinline__ double requant_m_ref(float x, float d, double lm) {
     double q = round((double)x / (double)d);
     const double lo = -lm, hi = lm - 1.0;
     if (q < lo) q = lo;
@@ -132,7 +132,7 @@ __device__ __noinline__ double requant_m_ref(float x, float d, double lm) {
 }
 
 // Reference expression for an unsigned (v) code, clamped to [0, L].
-__device__ __noinline__ double requant_v_ref(float x, float d, double lv) {
+static __device__ __noinline__ double requant_v_ref(float x, float d, double lv) {
     double q = round((double)x / (double)d);
     if (q < 0.0) q = 0.0;
     if (q > lv) q = lv;

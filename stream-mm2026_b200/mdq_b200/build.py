@@ -12,6 +12,8 @@ import os
 import shutil
 import subprocess
 import sys
+import tempfile
+from concurrent.futures import ThreadPoolExecutor
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 PKG_ROOT = os.path.dirname(PKG_DIR)                 # stream-mm2026_b200/
@@ -20,7 +22,8 @@ CSRC = os.path.join(PKG_ROOT, "csrc")
 INCLUDE = os.path.join(REPO_ROOT, "include")
 LIB_PATH = os.path.join(PKG_DIR, "libmdq.so")
 
-SOURCES = ["mdq_step.cu", "mdq_stats.cu"]
+SOURCES = ["mdq_step.cu", "mdq_stats.cu", "mdq_tiles_packed4.cu", "mdq_tiles_s8u8.cu",
+           "mdq_tiles_s16u16.cu", "mdq_tiles_s32u32.cu", "mdq_tiles_m8v4.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -46,17 +49,30 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Build libmdq.so unless it is newer than every source; return its path."""
+    """Build libmdq.so unless it is newer than every source; return its path.
+
+    Each translation unit compiles in its own nvcc process (in parallel),
+    then one nvcc call links the shared library."""
     if not force and up_to_date():
         return LIB_PATH
-    tmp = LIB_PATH + ".tmp"
-    cmd = [nvcc(), *GENCODE, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-           "-shared", f"-I{INCLUDE}", f"-I{CSRC}", "-o", tmp,
-           *[os.path.join(CSRC, s) for s in SOURCES]]
+    common = [nvcc(), *GENCODE, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+              f"-I{INCLUDE}", f"-I{CSRC}"]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd), flush=True)
-    subprocess.run(cmd, check=True)
+        common.insert(1, "-Xptxas=-v")
+    with tempfile.TemporaryDirectory(prefix="mdq_build_") as tmpdir:
+        objs = [os.path.join(tmpdir, os.path.splitext(src)[0] + ".o") for src in SOURCES]
+
+        def compile_one(i: int) -> None:
+            cmd = [*common, "-c", os.path.join(CSRC, SOURCES[i]), "-o", objs[i]]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            subprocess.run(cmd, check=True)
+
+        workers = max(1, min(len(SOURCES), os.cpu_count() or 1))
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            list(pool.map(compile_one, range(len(SOURCES))))
+        tmp = LIB_PATH + ".tmp"
+        subprocess.run([nvcc(), *GENCODE, "-shared", "-o", tmp, *objs], check=True)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 
