@@ -98,3 +98,36 @@ def test_state_dict_layout_and_getters(cpu_kernel):
         assert k in t
     m, v = opt.dequantized_moments(params[0])
     assert m.shape == (params[0].numel(),) and torch.isfinite(v).all()
+
+
+@pytest.mark.parametrize("name,cls", [("simple", optim.MDQAdamWSimple),
+                                      ("fusedio", optim.MDQAdamWSimpleFusedIO)])
+def test_resume_from_reference_written_checkpoint(cpu_kernel, name, cls):
+    """A checkpoint written by the reference's own class (params +
+    optimizer.state_dict(), tests/golden/make_checkpoint_golden.py) loads into
+    ours; continuing gives the reference's continuation bit for bit."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+    from make_checkpoint_golden import KW, MORE, SAVE_AT, groups
+    from host_scenario import SIZES
+
+    gdir = os.path.join(os.path.dirname(__file__), "golden")
+    ck = torch.load(os.path.join(gdir, f"ref_ckpt_{name}.pt"), weights_only=False)
+    ref = np.load(os.path.join(gdir, f"ref_ckpt_{name}_final.npz"))
+    params = [torch.nn.Parameter(t.clone()) for t in ck["params"]]
+    opt = cls(groups(params), **KW)
+    opt.load_state_dict(ck["optimizer"])
+    for t in range(SAVE_AT + 1, SAVE_AT + MORE + 1):
+        for p, g in zip(params, grads_for_step(SIZES, t)):
+            p.grad = g.clone()
+        opt.step()
+    assert opt.total_steps == int(ref["total_steps"])
+    for i, p in enumerate(params):
+        st = opt.state[p]
+        np.testing.assert_array_equal(p.detach().numpy().view(np.int32), ref[f"p{i}"].view(np.int32))
+        assert int(st["current_bit"]) == int(ref[f"bits{i}"]) and int(st["step"]) == int(ref[f"step{i}"])
+        for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
+            tt = st[k]
+            assert str(tt.dtype) == str(ref[f"{k}{i}_dtype"]), (i, k)
+            got = tt.view(torch.uint8).numpy() if tt.numel() else np.zeros(0, np.uint8)
+            np.testing.assert_array_equal(got, ref[f"{k}{i}"], err_msg=f"param {i} {k}")
