@@ -15,10 +15,15 @@ Layout.  Parameter i occupies [off_i, off_i + n_i) of the flat buffers, with
 off_i a multiple of the quantisation block B and the segment padded to a whole
 number of blocks, so a block never spans two parameters and a parameter's last
 (partial) block keeps the reference's tail semantics (CUDA/stquant_kernel.cu:
-92-97).  The flat length is padded to world * S with S a multiple of B; rank r
-owns [r*S, (r+1)*S).  A parameter may span ranks: each rank holds the pieces
-of it that fall in its shard, cut at block boundaries, so the sharded step
-computes exactly the codes, scales and parameters of the unsharded one.
+92-97).  Parameters are grouped in order into buckets (one by default); each
+bucket is padded to world * S with S a multiple of B, and rank r owns
+[base + r*S, base + (r+1)*S) of every bucket.  A parameter may span ranks:
+each rank holds the pieces of it that fall in its shards, cut at block
+boundaries, so the sharded step computes exactly the codes, scales and
+parameters of the unsharded one.  Buckets are the unit of communication: with
+``overlap_grad_reduce`` a bucket's reduce-scatter starts during backward, as
+soon as its last gradient is accumulated (the role DDP's bucketed all-reduce
+plays in baseline/pretrain_gpt.py:235).
 
 Bit policy.  The reference scores each tensor from torch reductions of its
 full gradient (CUDA/stquant_opt_simple.py:94-98).  No rank holds a full
@@ -30,6 +35,7 @@ other bit width; with ``fixed_bits`` the sharded step is bit-exact.
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 from typing import List, Optional
@@ -53,29 +59,69 @@ class Piece:
     flat_off: int
 
 
-class ShardLayout:
-    """Block-aligned placement of parameters in flat buffers and shards."""
+@dataclass
+class Bucket:
+    """Parameters [first, last) laid out in flat elements [base, base + world*shard)."""
 
-    def __init__(self, numels: List[int], block: int, world: int):
+    first: int
+    last: int
+    base: int
+    shard: int
+
+
+class ShardLayout:
+    """Block-aligned placement of parameters in flat buffers and shards.
+
+    Parameters are grouped, in order, into buckets of about ``bucket_elems``
+    elements (one bucket when None).  Each bucket is laid out on its own: every
+    parameter at a block-aligned offset, the bucket padded to world * shard
+    with shard a multiple of the block, rank r owning
+    [base + r*shard, base + (r+1)*shard).  Buckets are the unit of the
+    gradient reduce-scatter and the parameter all-gather."""
+
+    def __init__(self, numels: List[int], block: int, world: int,
+                 bucket_elems: Optional[int] = None):
         self.block = block
         self.world = world
         self.numels = list(numels)
-        self.offsets = []
-        off = 0
-        for n in numels:
-            self.offsets.append(off)
-            off += -(-n // block) * block
-        blocks = off // block
-        self.shard = -(-blocks // world) * block if blocks else block
-        self.total = self.shard * world
+        self.offsets = [0] * len(numels)
+        self.buckets: List[Bucket] = []
+        base, i = 0, 0
+        while i < len(numels) or not self.buckets:
+            first, off = i, 0
+            while i < len(numels):
+                padded = -(-numels[i] // block) * block
+                if bucket_elems is not None and i > first and off + padded > bucket_elems:
+                    break
+                self.offsets[i] = base + off
+                off += padded
+                i += 1
+            blocks = off // block
+            shard = -(-blocks // world) * block if blocks else block
+            self.buckets.append(Bucket(first, i, base, shard))
+            base += shard * world
+        self.total = base
+
+    @property
+    def shard(self) -> int:
+        """Shard length of a one-bucket layout."""
+        if len(self.buckets) != 1:
+            raise AttributeError("a bucketed layout has one shard length per bucket")
+        return self.buckets[0].shard
+
+    def shard_range(self, bucket: Bucket, rank: int):
+        lo = bucket.base + rank * bucket.shard
+        return lo, lo + bucket.shard
 
     def pieces(self, rank: int) -> List[Piece]:
-        lo, hi = rank * self.shard, (rank + 1) * self.shard
         out = []
-        for i, (off, n) in enumerate(zip(self.offsets, self.numels)):
-            a, b = max(off, lo), min(off + n, hi)
-            if a < b:
-                out.append(Piece(param=i, start=a - off, n=b - a, flat_off=a))
+        for b in self.buckets:
+            lo, hi = self.shard_range(b, rank)
+            for i in range(b.first, b.last):
+                off, n = self.offsets[i], self.numels[i]
+                a, e = max(off, lo), min(off + n, hi)
+                if a < e:
+                    out.append(Piece(param=i, start=a - off, n=e - a, flat_off=a))
         return out
 
 
@@ -83,14 +129,21 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
     """State-sharded MDQ-AdamW (FusedIO semantics per parameter piece).
 
     Arguments are those of the reference optimizer plus ``process_group``
-    (default: the world group) and ``grad_dtype`` (fp32 or bf16 flat
-    gradients).  The block is one per optimizer (``block_size``, clamped to
-    1024 unless ``exact_block``).
+    (default: the world group), ``grad_dtype`` (fp32 or bf16 flat gradients),
+    ``bucket_elems`` (reduce-scatter / all-gather granularity; one bucket when
+    None) and ``overlap_grad_reduce``: when set, each bucket's gradient
+    reduce-scatter is launched asynchronously from a post-accumulate-grad hook
+    as soon as backward has produced all of its gradients, so communication
+    overlaps the rest of backward; ``step()`` waits for them.  Inside
+    ``no_sync()`` (gradient accumulation) the hooks launch nothing.  The block
+    is one per optimizer (``block_size``, clamped to 1024 unless
+    ``exact_block``).
     """
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  alpha=0.9, layer_count=24, batch_size=32, update_freq=20, block_size=256,
-                 *, process_group=None, grad_dtype=torch.float32, **kw):
+                 *, process_group=None, grad_dtype=torch.float32, bucket_elems=None,
+                 overlap_grad_reduce=False, **kw):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                          alpha=alpha, layer_count=layer_count, batch_size=batch_size,
                          update_freq=update_freq, block_size=block_size, **kw)
@@ -107,7 +160,8 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             if p.dtype != torch.float32:
                 raise RuntimeError("MDQ parameters must be float32")
         dev = self.params[0].device
-        self.layout = ShardLayout([p.numel() for p in self.params], self.block, self.world)
+        self.layout = ShardLayout([p.numel() for p in self.params], self.block, self.world,
+                                  bucket_elems)
         self.flat_param = torch.zeros(self.layout.total, dtype=torch.float32, device=dev)
         self.flat_grad = torch.zeros(self.layout.total, dtype=grad_dtype, device=dev)
         for p, off in zip(self.params, self.layout.offsets):
@@ -118,15 +172,44 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
                 p.grad_dtype = grad_dtype  # low-precision gradients of fp32 parameters
             p.grad = self.flat_grad[off:off + n].view_as(p)
         self.pieces = self.layout.pieces(self.rank)
-        s = self.layout.shard
-        self.param_shard = self.flat_param[self.rank * s:(self.rank + 1) * s]
-        self.grad_shard = self.flat_grad[self.rank * s:(self.rank + 1) * s]
         self._descs = None
+        # Asynchronous bucket reduce-scatters launched during backward.
+        self._bucket_of = [0] * len(self.params)
+        for k, b in enumerate(self.layout.buckets):
+            for i in range(b.first, b.last):
+                self._bucket_of[i] = k
+        self._ready = [0] * len(self.layout.buckets)
+        self._works = [None] * len(self.layout.buckets)
+        self._sync = True
+        self._hooks = []
+        if overlap_grad_reduce and self.world > 1:
+            for i, p in enumerate(self.params):
+                self._hooks.append(p.register_post_accumulate_grad_hook(self._grad_ready(i)))
 
     # ------------------------------------------------------------------
     def zero_grad(self, set_to_none: bool = False):
         """Zero the flat gradient buffer (the views stay attached)."""
         self.flat_grad.zero_()
+
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backward passes inside accumulate gradients without communication."""
+        prev, self._sync = self._sync, False
+        try:
+            yield
+        finally:
+            self._sync = prev
+
+    def _grad_ready(self, i: int):
+        def hook(_p):
+            if not self._sync:
+                return
+            k = self._bucket_of[i]
+            self._ready[k] += 1
+            b = self.layout.buckets[k]
+            if self._ready[k] == b.last - b.first and self._works[k] is None:
+                self._works[k] = self._reduce_scatter_bucket(b, async_op=True)
+        return hook
 
     def _piece_state(self, pc: Piece):
         """State of one local piece, initialised as the reference initialises
@@ -134,7 +217,7 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         p = self.params[pc.param]
         st = self.state[p]
         if len(st) == 0:
-            proxy = self.param_shard[pc.flat_off - self.rank * self.layout.shard:][:pc.n]
+            proxy = self.flat_param[pc.flat_off:pc.flat_off + pc.n]
             nb = -(-pc.n // self.block)
             st["step"] = 0
             if self.fixed_bits is None:
@@ -153,29 +236,50 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         return st
 
     def _piece_views(self, pc: Piece):
-        o = pc.flat_off - self.rank * self.layout.shard
-        return self.param_shard[o:o + pc.n], self.grad_shard[o:o + pc.n]
+        a, e = pc.flat_off, pc.flat_off + pc.n
+        return self.flat_param[a:e], self.flat_grad[a:e]
 
     # ------------------------------------------------------------------
+    def _reduce_scatter_bucket(self, b: Bucket, async_op: bool = False):
+        """Average one bucket's gradients onto its shard owners (in place)."""
+        full = self.flat_grad[b.base:b.base + b.shard * self.world]
+        if dist.get_backend(self.group) == "nccl":
+            lo, hi = self.layout.shard_range(b, self.rank)
+            return dist.reduce_scatter_tensor(self.flat_grad[lo:hi], full, op=dist.ReduceOp.AVG,
+                                              group=self.group, async_op=async_op)
+        # gloo has no reduce-scatter: all-reduce (the average is taken once
+        # the sum is complete), then every rank reads its shard.
+        return dist.all_reduce(full, group=self.group, async_op=async_op)
+
+    def _finish_bucket(self, b: Bucket):
+        if dist.get_backend(self.group) != "nccl":
+            self.flat_grad[b.base:b.base + b.shard * self.world].div_(self.world)
+
     def _reduce_scatter_grads(self):
         if self.world == 1:
             return
-        if dist.get_backend(self.group) == "nccl":
-            dist.reduce_scatter_tensor(self.grad_shard, self.flat_grad, op=dist.ReduceOp.AVG,
-                                       group=self.group)
-        else:
-            # gloo has no reduce-scatter: all-reduce, then every rank reads its shard.
-            dist.all_reduce(self.flat_grad, group=self.group)
-            self.flat_grad.div_(self.world)
+        for k, b in enumerate(self.layout.buckets):
+            w = self._works[k]
+            if w is None:
+                self._reduce_scatter_bucket(b)
+            else:
+                w.wait()
+            self._finish_bucket(b)
+            self._works[k] = None
+            self._ready[k] = 0
 
     def _all_gather_params(self):
         if self.world == 1:
             return
-        if dist.get_backend(self.group) == "nccl":
-            dist.all_gather_into_tensor(self.flat_param, self.param_shard, group=self.group)
-        else:
-            parts = list(self.flat_param.chunk(self.world))
-            dist.all_gather(parts, self.param_shard.clone(), group=self.group)
+        nccl = dist.get_backend(self.group) == "nccl"
+        for b in self.layout.buckets:
+            full = self.flat_param[b.base:b.base + b.shard * self.world]
+            lo, hi = self.layout.shard_range(b, self.rank)
+            if nccl:
+                dist.all_gather_into_tensor(full, self.flat_param[lo:hi], group=self.group)
+            else:
+                parts = list(full.chunk(self.world))
+                dist.all_gather(parts, self.flat_param[lo:hi].clone(), group=self.group)
 
     def _global_grad_stats(self):
         """Per-parameter [n_l, r_l, v_l] from all-reduced partial sums."""

@@ -1,6 +1,7 @@
 """ZeRO-1 on real GPUs with NCCL (needs >= 2 devices; skipped otherwise):
 reduce-scatter / fused step / all-gather equals the unsharded optimizer on one
-GPU with the averaged gradients, bit for bit (fixed bit widths, exact p)."""
+GPU with the averaged gradients, bit for bit (fixed bit widths, exact p), also
+with bucketed reduce-scatters launched during backward."""
 import os
 import socket
 
@@ -29,7 +30,7 @@ def _params(device):
 KW = dict(lr=1e-3, weight_decay=0.01, block_size=256, p_mode="exact")
 
 
-def _worker(rank, world, port, steps, bits, q):
+def _worker(rank, world, port, steps, bits, overlap, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
@@ -38,12 +39,19 @@ def _worker(rank, world, port, steps, bits, q):
         from mdq_b200.zero1 import ZeroMDQAdamW
 
         params = _params(torch.device("cuda", rank))
+        extra = dict(bucket_elems=300_000, overlap_grad_reduce=True) if overlap else {}
         opt = ZeroMDQAdamW([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
-                           fixed_bits=bits, **KW)
+                           fixed_bits=bits, **KW, **extra)
         for t in range(1, steps + 1):
             opt.zero_grad()
-            for p, g in zip(params, _grads(rank, t)):
-                p.grad.copy_(g)
+            if overlap:
+                # Gradients from backward (loss = sum_i <p_i, c_i>): the bucket
+                # reduce-scatters start from the hooks, during backward.
+                coef = [c.to(params[0].device) for c in _grads(rank, t)]
+                sum((p * c).sum() for p, c in zip(params, coef)).backward()
+            else:
+                for p, g in zip(params, _grads(rank, t)):
+                    p.grad.copy_(g)
             opt.step()
         torch.cuda.synchronize()
         sd = opt.consolidated_state_dict()
@@ -55,8 +63,8 @@ def _worker(rank, world, port, steps, bits, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("bits", [4, (8, 4), 8])
-def test_zero1_nccl_equals_unsharded(cuda_device, bits):
+@pytest.mark.parametrize("bits,overlap", [(4, False), ((8, 4), False), (8, False), ((8, 4), True)])
+def test_zero1_nccl_equals_unsharded(cuda_device, bits, overlap):
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs at least two GPUs")
@@ -76,7 +84,7 @@ def test_zero1_nccl_equals_unsharded(cuda_device, bits):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, bits, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, bits, overlap, q))
              for r in range(world)]
     for p in procs:
         p.start()

@@ -101,15 +101,20 @@ def _run_sharded(world, steps, kw, sizes):
     return out
 
 
-def test_layout_is_block_aligned_and_covers_every_element():
+@pytest.mark.parametrize("bucket_elems", [None, 1, 3000])
+def test_layout_is_block_aligned_and_covers_every_element(bucket_elems):
     for world in (1, 2, 3, 8):
-        lay = ShardLayout(SIZES, 256, world)
+        lay = ShardLayout(SIZES, 256, world, bucket_elems)
         assert lay.total % (world * 256) == 0
+        if bucket_elems == 1:
+            assert len(lay.buckets) == len(SIZES)
         seen = {i: 0 for i in range(len(SIZES))}
         for r in range(world):
             for pc in lay.pieces(r):
                 assert pc.flat_off % 256 == 0 and pc.start % 256 == 0
-                assert r * lay.shard <= pc.flat_off and pc.flat_off + pc.n <= (r + 1) * lay.shard
+                b = next(b for b in lay.buckets if b.first <= pc.param < b.last)
+                lo, hi = lay.shard_range(b, r)
+                assert lo <= pc.flat_off and pc.flat_off + pc.n <= hi
                 seen[pc.param] += pc.n
         assert [seen[i] for i in range(len(SIZES))] == SIZES
 
@@ -231,3 +236,65 @@ def test_checkpoint_resharding_resume(w_save, w_resume, kw):
         for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
             np.testing.assert_array_equal(rs[k].numpy().view(np.uint8),
                                           st[k].numpy().view(np.uint8), err_msg=f"param {i} {k}")
+
+
+def _overlap_worker(rank, world, port, steps, kw, sizes, q):
+    """Gradients from real backward passes (loss = sum_i <p_i, c_i>, so the
+    gradient is exactly c_i): two micro-batches per step, the first inside
+    no_sync(); bucket reduce-scatters launched from the hooks."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _use_oracle()
+        from mdq_b200.zero1 import ZeroMDQAdamW
+
+        torch.set_num_threads(1)
+        params = _params(sizes)
+        opt = ZeroMDQAdamW([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
+                           lr=1e-3, weight_decay=0.01, block_size=256, bucket_elems=3000,
+                           overlap_grad_reduce=True, **kw)
+        assert len(opt.layout.buckets) > 2
+        for t in range(1, steps + 1):
+            opt.zero_grad()
+            coef = _grads(rank, t, sizes)
+            with opt.no_sync():
+                sum((p * (c / 2)).sum() for p, c in zip(params, coef)).backward()
+            assert all(w is None for w in opt._works)
+            sum((p * (c / 2)).sum() for p, c in zip(params, coef)).backward()
+            assert all(w is not None for w in opt._works)  # launched during backward
+            opt.step()
+        sd = opt.consolidated_state_dict()
+        if rank == 0:
+            q.put(([p.detach().numpy().copy() for p in params],
+                   {i: {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in st.items()}
+                    for i, st in sd["state"].items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,kw", [(2, dict(fixed_bits=(8, 4))), (3, dict())])
+def test_bucketed_overlap_equals_unsharded(world, kw):
+    steps = 4
+    sizes = SIZES if kw else [n for n in SIZES if n > 1]
+    ref_params, ref_opt = _unsharded(world, steps, kw, sizes)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_overlap_worker, args=(r, world, port, steps, kw, sizes, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    params, state = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for i, (a, b) in enumerate(zip(ref_params, params)):
+        np.testing.assert_array_equal(a.detach().numpy().view(np.int32), b.view(np.int32),
+                                      err_msg=f"param {i}")
+    for i, p in enumerate(ref_params):
+        rs, st = ref_opt.state[p], state[i]
+        assert st["step"] == rs["step"] and st["current_bit"] == rs["current_bit"], i
+        for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
+            np.testing.assert_array_equal(rs[k].numpy().view(np.uint8), st[k].view(np.uint8),
+                                          err_msg=f"param {i} {k}")
