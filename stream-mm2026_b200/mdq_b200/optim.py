@@ -389,6 +389,58 @@ class MDQAdamWSimple(Optimizer):
         """Float m and v of one parameter, decoded from its codes and scales."""
         return dequantize_state(self.state[p], p.numel(), self._block_of(self._group_of(p)))
 
+    def quant_error(self, block_size=None) -> float:
+        """Relative L2 quantisation error of the moments, the training script's
+        metric (baseline/pretrain_gpt.py:88-104): every parameter's float
+        m and v (decoded from its codes) are fake-quantised at its current bit
+        width with ``robust_quantize`` (blocks of ``block_size``, default the
+        group's block), and sqrt(sum |x - q(x)|^2 / (sum |x|^2 + 1e-12)) is
+        returned.  The sums stay on the parameters' device; one host read."""
+        num = den = None
+        for group in self.param_groups:
+            blk = block_size or self._block_of(group)
+            for p in group["params"]:
+                st = self.state.get(p)
+                if not st or "exp_avg" not in st:
+                    continue
+                bit = int(st.get("current_bit", 32))
+                m, v = self.dequantized_moments(p)
+                qm = self.robust_quantize(m, bit, is_v=False, block_size=blk)
+                qv = self.robust_quantize(v, bit, is_v=True, block_size=blk)
+                a = (m - qm).pow(2).sum() + (v - qv).pow(2).sum()
+                b = m.pow(2).sum() + v.pow(2).sum()
+                num = a if num is None else num + a
+                den = b if den is None else den + b
+        if num is None:
+            return 0.0
+        return float(torch.sqrt(num / (den + 1e-12)))
+
+    def robust_quantize(self, tensor, bits, is_v=False, block_size=2048):
+        """Fake-quantise a float tensor (baseline/mdqbock_newhook.py:58-83)."""
+        if bits >= 31:
+            return tensor
+        orig_shape = tensor.shape
+        flat = tensor.flatten()
+        numel = flat.numel()
+        pad_len = (block_size - (numel % block_size)) % block_size
+        padded = torch.nn.functional.pad(flat, (0, pad_len)) if pad_len > 0 else flat
+        blocked = padded.view(-1, block_size)
+        eps = 1e-12
+        if is_v:
+            log_v = torch.log(blocked + eps)
+            v_max = log_v.max(dim=1, keepdim=True)[0]
+            v_min = log_v.min(dim=1, keepdim=True)[0]
+            scale = (v_max - v_min) / (2 ** bits - 1)
+            q = torch.round((log_v - v_min) / (scale + eps)).clamp(0, 2 ** bits - 1)
+            deq = torch.exp(q * scale + v_min)
+        else:
+            q_levels = 2 ** (bits - 1)
+            max_val = blocked.abs().max(dim=1, keepdim=True)[0]
+            scale = (max_val + eps) / (q_levels - 1)
+            q = torch.round(blocked / (scale + eps)).clamp(-q_levels, q_levels - 1)
+            deq = q * scale
+        return deq.view(-1)[:numel].view(orig_shape)
+
     def _group_of(self, p):
         for g in self.param_groups:
             if any(q is p for q in g["params"]):
@@ -579,7 +631,8 @@ class MDQAdamWSimpleFusedIO(MDQAdamWSimple):
 class MDQAdamW(MDQAdamWSimpleFusedIO):
     """Drop-in for ``baseline/mdqbock_newhook.py:MDQAdamW`` as used by
     ``baseline/pretrain_gpt.py:192-198``: same constructor defaults, state in
-    low-bit codes instead of fp32 moments, plus ``robust_quantize``."""
+    low-bit codes instead of fp32 moments (``robust_quantize`` and
+    ``quant_error`` come with every class here)."""
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  alpha=0.9, layer_count=12, batch_size=8, update_freq=20, block_size=2048,
@@ -587,32 +640,6 @@ class MDQAdamW(MDQAdamWSimpleFusedIO):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                          alpha=alpha, layer_count=layer_count, batch_size=batch_size,
                          update_freq=update_freq, block_size=block_size, **kw)
-
-    def robust_quantize(self, tensor, bits, is_v=False, block_size=2048):
-        """Fake-quantise a float tensor (baseline/mdqbock_newhook.py:58-83)."""
-        if bits >= 31:
-            return tensor
-        orig_shape = tensor.shape
-        flat = tensor.flatten()
-        numel = flat.numel()
-        pad_len = (block_size - (numel % block_size)) % block_size
-        padded = torch.nn.functional.pad(flat, (0, pad_len)) if pad_len > 0 else flat
-        blocked = padded.view(-1, block_size)
-        eps = 1e-12
-        if is_v:
-            log_v = torch.log(blocked + eps)
-            v_max = log_v.max(dim=1, keepdim=True)[0]
-            v_min = log_v.min(dim=1, keepdim=True)[0]
-            scale = (v_max - v_min) / (2 ** bits - 1)
-            q = torch.round((log_v - v_min) / (scale + eps)).clamp(0, 2 ** bits - 1)
-            deq = torch.exp(q * scale + v_min)
-        else:
-            q_levels = 2 ** (bits - 1)
-            max_val = blocked.abs().max(dim=1, keepdim=True)[0]
-            scale = (max_val + eps) / (q_levels - 1)
-            q = torch.round(blocked / (scale + eps)).clamp(-q_levels, q_levels - 1)
-            deq = q * scale
-        return deq.view(-1)[:numel].view(orig_shape)
 
 
 # ----------------------------------------------------------------------

@@ -131,3 +131,25 @@ def test_resume_from_reference_written_checkpoint(cpu_kernel, name, cls):
             assert str(tt.dtype) == str(ref[f"{k}{i}_dtype"]), (i, k)
             got = tt.view(torch.uint8).numpy() if tt.numel() else np.zeros(0, np.uint8)
             np.testing.assert_array_equal(got, ref[f"{k}{i}"], err_msg=f"param {i} {k}")
+
+
+def test_quant_error_is_the_training_scripts_metric(cpu_kernel):
+    """quant_error() == the reference script's compute_mdq_quant_error
+    (baseline/pretrain_gpt.py:88-104, restated here) over the decoded moments."""
+    from host_scenario import SIZES
+    params = make_params(SIZES)
+    opt = _run(optim.MDQAdamWSimpleFusedIO, params, 6)
+    num = den = 0.0
+    for group in opt.param_groups:
+        for p in group["params"]:
+            st = opt.state[p]
+            bit = st.get("current_bit", 32)
+            m, v = opt.dequantized_moments(p)
+            qm = opt.robust_quantize(m, bit, is_v=False, block_size=256)
+            qv = opt.robust_quantize(v, bit, is_v=True, block_size=256)
+            num += (m - qm).pow(2).sum().item() + (v - qv).pow(2).sum().item()
+            den += m.pow(2).sum().item() + v.pow(2).sum().item()
+    want = (num / (den + 1e-12)) ** 0.5
+    got = opt.quant_error()
+    assert 0.0 < got < 1.0
+    assert abs(got - want) <= 1e-5 * want
