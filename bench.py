@@ -14,6 +14,7 @@ has no data-path collective), so scaling is weak and `value` is the whole
 job's parameters per second: N * 2^30 / (max over ranks of the step time).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--bits 4|8] [--block B] [--log2-elements k]   (other config-2 points)
 
 Prints one JSON line (rank 0).
 """
@@ -42,13 +43,18 @@ HP = dict(lr=1e-3, weight_decay=0.01, eps=1e-8, beta1=0.9, beta2=0.999)
 # Algorithmic bytes per element: p read+write 8, bf16 grad 2, packed4 code
 # read+write 2, and three fp32 scales read+written per block.
 BYTES_PER_ELEM = 8 + 2 + 2 + 3 * 4 * 2 / BLOCK
+BITS = 4                                 # --bits 8: int8 m / uint8 v codes (2 B read+written)
 SPEC_HBM_GBS = 8000.0
 
 
+def layout_name():
+    return "packed 4-bit m/v" if BITS == 4 else "int8 m / uint8 v codes"
+
+
 def config(n_gpus: int) -> dict:
-    return {"workload": f"flat fp32 tensor 2^{LOG2_N} elts/GPU, packed 4-bit m/v, bf16 grads, "
+    return {"workload": f"flat fp32 tensor 2^{LOG2_N} elts/GPU, {layout_name()}, bf16 grads, "
                         f"block {BLOCK_REQUESTED} (quantised per {BLOCK} as the reference)",
-            "elements_per_gpu": 1 << LOG2_N, "bits": 4, "block_requested": BLOCK_REQUESTED,
+            "elements_per_gpu": 1 << LOG2_N, "bits": BITS, "block_requested": BLOCK_REQUESTED,
             "quant_block": BLOCK, "grad_dtype": "bf16", "param_dtype": "fp32",
             "parallelism": f"zero1-state-shard x{n_gpus}" if n_gpus > 1 else "single",
             "l2": f"inputs larger than L2 ({(1 << LOG2_N) * 7 / 2**30:.1f} GiB/GPU), no flush"}
@@ -122,11 +128,21 @@ def make_state(n, device, seed):
     p = torch.randn(n, device=device, generator=g) * 0.02
     grad = (torch.randn(n, device=device, generator=g) * 1e-3).to(torch.bfloat16)
     nb = (n + BLOCK - 1) // BLOCK
-    codes = torch.full((n,), 8, dtype=torch.uint8, device=device)
+    if BITS == 4:
+        codes = (torch.full((n,), 8, dtype=torch.uint8, device=device), None)
+    else:
+        codes = (torch.zeros(n, dtype=torch.int8, device=device),
+                 torch.zeros(n, dtype=torch.uint8, device=device))
     sm = torch.zeros(nb, device=device)
     sv = torch.zeros(nb, device=device)
     vmin = torch.full((nb,), -20.0, device=device)
     return p, grad, codes, sm, sv, vmin
+
+
+def code_layout():
+    from mdq_b200.kernels import LAYOUT_PACKED4, LAYOUT_S8U8
+
+    return LAYOUT_PACKED4 if BITS == 4 else LAYOUT_S8U8
 
 
 def run_ours(args, rank, world, local_rank):
@@ -135,15 +151,15 @@ def run_ours(args, rank, world, local_rank):
 
     from mdq_b200 import kernels
     from mdq_b200._lib import TensorDesc
-    from mdq_b200.kernels import LAYOUT_PACKED4, P_FAST, StepItem
+    from mdq_b200.kernels import P_FAST, StepItem
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     n = 1 << LOG2_N
     p, grad, codes, sm, sv, vmin = make_state(n, device, seed=rank)
-    item = StepItem(p=p, grad=grad, exp_avg=codes, exp_avg_sq=None, scale_m=sm, scale_v=sv,
-                    v_min=vmin, step=1, block=BLOCK, m_bits=4, v_bits=4,
-                    layout=LAYOUT_PACKED4, **HP)
+    item = StepItem(p=p, grad=grad, exp_avg=codes[0], exp_avg_sq=codes[1], scale_m=sm,
+                    scale_v=sv, v_min=vmin, step=1, block=BLOCK, m_bits=BITS, v_bits=BITS,
+                    layout=code_layout(), **HP)
     descs = (TensorDesc * 1)()
     stream = torch.cuda.current_stream(device)
 
@@ -217,7 +233,7 @@ def run_e2e(args, device, p, grad, codes, sm, sv, vmin, t0):
     import torch
 
     from mdq_b200 import kernels
-    from mdq_b200.kernels import LAYOUT_PACKED4, P_FAST, StepItem
+    from mdq_b200.kernels import P_FAST, StepItem
 
     n = p.numel()
     chunk = 1 << 26
@@ -231,9 +247,10 @@ def run_e2e(args, device, p, grad, codes, sm, sv, vmin, t0):
     for c in range(nchunks):
         sl = slice(c * chunk, (c + 1) * chunk)
         bs = slice(c * cpb, (c + 1) * cpb)
-        items.append(StepItem(p=p[sl], grad=grad[sl], exp_avg=codes[sl], exp_avg_sq=None,
+        items.append(StepItem(p=p[sl], grad=grad[sl], exp_avg=codes[0][sl],
+                              exp_avg_sq=None if codes[1] is None else codes[1][sl],
                               scale_m=sm[bs], scale_v=sv[bs], v_min=vmin[bs], step=1, block=BLOCK,
-                              m_bits=4, v_bits=4, layout=LAYOUT_PACKED4, **HP))
+                              m_bits=BITS, v_bits=BITS, layout=code_layout(), **HP))
 
     def one_step(t):
         done_h2d = []
@@ -327,7 +344,8 @@ def run_zero1(args, rank, world, device):
 def traffic_per_launch(n_elems):
     """DRAM bytes per launch from the committed ncu summary of this kernel,
     scaled from its capture size to this launch (traffic is proportional)."""
-    path = os.path.join(REPO, "profiles", f"mdq_step_tiles_packed4_bf16_b{BLOCK}.json")
+    lay = "packed4" if BITS == 4 else "s8u8"
+    path = os.path.join(REPO, "profiles", f"mdq_step_tiles_{lay}_bf16_b{BLOCK}.json")
     try:
         with open(path) as f:
             d = json.load(f)
@@ -351,7 +369,10 @@ def cpu_baseline(budget_s=12.0, threads=None):
     rng = np.random.default_rng(0)
     p = (rng.standard_normal(n) * 0.02).astype(np.float32)
     g = (rng.standard_normal(n) * 1e-3).astype(np.float32)
-    codes = np.full(n, 8, np.uint8)
+    if BITS == 4:
+        codes, vcodes, lay = np.full(n, 8, np.uint8), None, oracle.LAYOUT_PACKED4
+    else:
+        codes, vcodes, lay = np.zeros(n, np.int8), np.zeros(n, np.uint8), oracle.LAYOUT_S8U8
     nb = n // BLOCK
     sm = np.zeros(nb, np.float32)
     sv = np.zeros(nb, np.float32)
@@ -360,15 +381,15 @@ def cpu_baseline(budget_s=12.0, threads=None):
     t0 = time.perf_counter()
     while True:
         steps += 1
-        oracle.step(p, g, oracle.LAYOUT_PACKED4, codes, None, sm, sv, vmin, BLOCK, HP["beta1"],
-                    HP["beta2"], HP["lr"], HP["weight_decay"], HP["eps"], steps, 4, 4,
+        oracle.step(p, g, lay, codes, vcodes, sm, sv, vmin, BLOCK, HP["beta1"],
+                    HP["beta2"], HP["lr"], HP["weight_decay"], HP["eps"], steps, BITS, BITS,
                     threads=threads)
         t = time.perf_counter() - t0
         if (t >= budget_s and steps >= 3) or steps >= 2000:
             break
     return {"value": round(n * steps / t / 1e9, 4), "unit": UNIT, "cores": threads,
             "kind": "port",
-            "sample": f"{steps} steps x 2^22 elements (oracle/mdq_oracle.c, packed 4-bit, "
+            "sample": f"{steps} steps x 2^22 elements (oracle/mdq_oracle.c, {layout_name()}, "
                       f"block {BLOCK}, fp32 grads) in {t:.1f} s"}
 
 
@@ -401,11 +422,13 @@ def main() -> int:
                     help="elements per GPU = 2^k (profiling cases use smaller k)")
     ap.add_argument("--block", type=int, default=2048,
                     help="requested block; quantised per min(block, 1024) as the reference")
+    ap.add_argument("--bits", type=int, default=4, choices=[4, 8],
+                    help="code width of m and v (4: packed layout, 8: int8 / uint8)")
     args = ap.parse_args()
-    global LOG2_N, BLOCK_REQUESTED, BLOCK, BYTES_PER_ELEM
-    LOG2_N, BLOCK_REQUESTED = args.log2_elements, args.block
+    global LOG2_N, BLOCK_REQUESTED, BLOCK, BYTES_PER_ELEM, BITS
+    LOG2_N, BLOCK_REQUESTED, BITS = args.log2_elements, args.block, args.bits
     BLOCK = min(BLOCK_REQUESTED, 1024)
-    BYTES_PER_ELEM = 8 + 2 + 2 + 3 * 4 * 2 / BLOCK
+    BYTES_PER_ELEM = 8 + 2 + (2 if BITS == 4 else 4) + 3 * 4 * 2 / BLOCK
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
