@@ -316,9 +316,10 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     for (int k = 0; k < PT; ++k) x[k] = (FULL || (k & 3) < cnt[k / 4]) ? __fadd_rn(v[k], 1e-12f) : 1.0f;
     float s0 = kNaN, s1 = kNaN, s2 = kNaN;
 #pragma unroll
-    for (int k = 0; k < PT; ++k) {
-        const bool ok = FULL || (k & 3) < cnt[k / 4];
-        s0 = fmaxf(s0, ok ? fabsf(m[k]) : 0.0f);
+    for (int k = 0; k < PT; k += 2) {
+        const bool ok0 = FULL || (k & 3) < cnt[k / 4];
+        const bool ok1 = FULL || ((k + 1) & 3) < cnt[k / 4];
+        s0 = max3f(s0, ok0 ? fabsf(m[k]) : 0.0f, ok1 ? fabsf(m[k + 1]) : 0.0f);
     }
 #pragma unroll
     for (int k = 0; k < PT; k += 2) {
