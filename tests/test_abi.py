@@ -117,3 +117,40 @@ def test_product_has_no_cpu_path():
                                 torch.zeros(10, dtype=torch.uint8), torch.zeros(1),
                                 torch.zeros(1), torch.zeros(1), 0.9, 0.999, 1e-3, 0.0, 1e-8,
                                 1, 8, 256)
+
+
+def test_descriptor_packing_matches_the_ctypes_mirror():
+    """fill_desc packs mdq_tensor_desc with struct.pack_into: every field must
+    land where the ctypes mirror (and so the C header) has it."""
+    import ctypes
+
+    import torch
+
+    from mdq_b200 import kernels
+    from mdq_b200._lib import TensorDesc
+
+    assert kernels._DESC_FMT.size <= ctypes.sizeof(TensorDesc)
+    expect_off = {"p": 0, "grad": 8, "exp_avg": 16, "exp_avg_sq": 24, "scale_m": 32, "scale_v": 40,
+                  "v_min": 48, "n": 56, "step": 64, "block": 68, "lr": 72, "weight_decay": 76,
+                  "eps": 80, "beta1": 84, "beta2": 88, "m_bits": 92, "v_bits": 96, "layout": 100,
+                  "grad_dtype": 104}
+    for name, off in expect_off.items():
+        assert getattr(TensorDesc, name).offset == off, name
+    p = torch.zeros(1000)
+    t = [torch.zeros(1000, dtype=torch.uint8), torch.zeros(4), torch.zeros(4), torch.zeros(4)]
+    for easq in (None, torch.zeros(1000, dtype=torch.uint8)):
+        it = kernels.StepItem(p=p, grad=torch.zeros(1000, dtype=torch.bfloat16), exp_avg=t[0],
+                              exp_avg_sq=easq, scale_m=t[1], scale_v=t[2], v_min=t[3], step=7,
+                              block=256, lr=3e-4, weight_decay=0.1, eps=1e-8, beta1=0.9,
+                              beta2=0.95, m_bits=8, v_bits=4, layout=4)
+        d = TensorDesc()
+        kernels.fill_desc(d, it)
+        assert (d.p, d.grad, d.exp_avg, d.scale_m, d.scale_v, d.v_min) == (
+            p.data_ptr(), it.grad.data_ptr(), t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(),
+            t[3].data_ptr())
+        assert (d.exp_avg_sq or 0) == (easq.data_ptr() if easq is not None else 0)
+        assert (d.n, d.step, d.block, d.m_bits, d.v_bits, d.layout) == (1000, 7, 256, 8, 4, 4)
+        assert d.grad_dtype == kernels._DTYPE_CODE[torch.bfloat16]
+        for name, val in (("lr", 3e-4), ("weight_decay", 0.1), ("eps", 1e-8), ("beta1", 0.9),
+                          ("beta2", 0.95)):
+            assert getattr(d, name) == ctypes.c_float(val).value, name
