@@ -8,6 +8,7 @@ Public API:
 """
 from .kernels import StepItem, fused_mdq_adamw, step_multi  # noqa: F401
 from .optim import MDQAdamW, MDQAdamWSimple, MDQAdamWSimpleFusedIO  # noqa: F401
+from .zero1 import ZeroMDQAdamW  # noqa: F401
 
 __all__ = ["MDQAdamW", "MDQAdamWSimple", "MDQAdamWSimpleFusedIO", "fused_mdq_adamw",
-           "step_multi", "StepItem"]
+           "step_multi", "StepItem", "ZeroMDQAdamW"]
