@@ -174,8 +174,11 @@ mdq_status mdq_grad_stats_multi(const void* const* grads, const int64_t* counts,
  * one per 65536 elements of each tensor (sum over tensors of
  * ceil(count / 65536)), and larger calls fail with MDQ_ERR_TOO_LARGE.  The
  * first call on each device looks up the array's device address (with that
- * device current); make that first call before any stream capture.  Calls
- * share the array: calls that overlap on the GPU race.  Allocates nothing.
+ * device current); make that first call before any stream capture.  The
+ * address is kept per device together with the id of the context it belongs
+ * to, and looked up again when that context has been replaced (a device
+ * reset).  Calls share the array: calls that overlap on the GPU race.
+ * Allocates nothing.
  */
 mdq_status mdq_grad_stats_multi_noalloc(const void* const* grads, const int64_t* counts,
                                         int32_t n_tensors, int32_t grad_dtype, double* out,

@@ -18,17 +18,69 @@ On the GPU box the resulting ``oracle/_ref/stquant_timetest_cpp*.so`` is the
 bit-exact oracle for codes and block scales: the kernel under test is compared
 against the reference's own arithmetic, CUDA libm included.
 
-Usage:  python oracle/build_ref.py [--reference /path/to/reference]
+The reference's pure-PyTorch optimizer (``baseline/mdqbock_newhook.py``) and
+its two CUDA optimizer classes (``CUDA/stquant_opt_simple.py``,
+``CUDA/stquant_opt_fused_io.py``) are byte-compiled the same way: each is
+compiled where it lies into a sourceless ``oracle/_ref/<module>.pyc`` (same
+interpreter as the GPU box), so the GPU box, which has no reference checkout,
+can import and run the reference's own unmodified classes beside ours (the
+timed CPU baseline of ``bench.py --impl reference`` and the GPU parity tests).
+
+The checkout is found from ``--reference``, else ``MDQ_REFERENCE_ROOT``, else
+the ``reference_path`` that ``BASELINE.json`` records.
+
+Usage:  python oracle/build_ref.py [--reference PATH]
 """
 from __future__ import annotations
 
 import argparse
+import json
 import os
+import py_compile
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 MODULE = "stquant_timetest_cpp"
+
+
+REPO = os.path.dirname(HERE)
+# (module name, path within the reference checkout)
+PY_MODULES = (("mdqbock_newhook", os.path.join("baseline", "mdqbock_newhook.py")),
+              ("stquant_opt_simple", os.path.join("CUDA", "stquant_opt_simple.py")),
+              ("stquant_opt_fused_io", os.path.join("CUDA", "stquant_opt_fused_io.py")))
+
+
+def reference_root(explicit: str | None = None) -> str | None:
+    """The reference checkout: explicit argument, MDQ_REFERENCE_ROOT, or
+    BASELINE.json's ``reference_path``; None when none of them exists."""
+    cands = [explicit, os.environ.get("MDQ_REFERENCE_ROOT")]
+    try:
+        with open(os.path.join(REPO, "BASELINE.json")) as f:
+            cands.append(json.load(f).get("reference_path"))
+    except (OSError, ValueError):
+        pass
+    for c in cands:
+        if c and os.path.isdir(os.path.join(c, "CUDA")):
+            return c
+    return None
+
+
+def python_modules_built() -> bool:
+    return all(os.path.isfile(os.path.join(OUT_DIR, m + ".pyc")) for m, _ in PY_MODULES)
+
+
+def stage_python(reference_root: str) -> list[str]:
+    """Byte-compile the reference's optimizer modules into oracle/_ref."""
+    os.makedirs(OUT_DIR, exist_ok=True)
+    out = []
+    for mod, rel in PY_MODULES:
+        src = os.path.join(reference_root, rel)
+        dst = os.path.join(OUT_DIR, mod + ".pyc")
+        py_compile.compile(src, cfile=dst, doraise=True,
+                           invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
+        out.append(dst)
+    return out
 
 
 def built_module_path() -> str | None:
@@ -68,15 +120,20 @@ def build(reference_root: str, verbose: bool = False) -> str:
     path = built_module_path()
     if path is None:
         raise RuntimeError("reference extension did not build")
+    stage_python(reference_root)
     return path
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("MDQ_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=None,
+                    help="reference checkout (default: MDQ_REFERENCE_ROOT, else BASELINE.json)")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
-    print(build(a.reference, a.verbose))
+    root = reference_root(a.reference)
+    if root is None:
+        ap.error("reference checkout not found: pass --reference or set MDQ_REFERENCE_ROOT")
+    print(build(root, a.verbose))
     return 0
 
 

@@ -146,7 +146,36 @@ void mdq_clear_error();
 
 namespace {
 
-int64_t chunks_of(int64_t n) { return (n + mdq_stats::kChunk - 1) / mdq_stats::kChunk; }
+// ceil(n / kChunk) without forming n + kChunk - 1 (no overflow near INT64_MAX).
+int64_t chunks_of(int64_t n) {
+    return n / mdq_stats::kChunk + (n % mdq_stats::kChunk != 0 ? 1 : 0);
+}
+
+// Checks every argument and every launch group before anything is launched,
+// so a failing call leaves `out` untouched.  Returns the total number of
+// partial records (chunks) the call needs.
+mdq_status validate_stats_call(const void* const* grads, const int64_t* counts, int32_t n_tensors,
+                               int64_t* total_chunks) {
+    using mdq_stats::kCap;
+    int64_t total = 0;
+    for (int b = 0; b < n_tensors; b += kCap) {
+        const int cnt = n_tensors - b < kCap ? n_tensors - b : kCap;
+        int64_t c = 0;
+        for (int i = 0; i < cnt; ++i) {
+            const int64_t n = counts[b + i];
+            if (n < 0) return mdq_fail(MDQ_ERR_INVALID_ARG, "tensor %d: negative count", b + i);
+            if (grads != nullptr && n > 0 && grads[b + i] == nullptr)
+                return mdq_fail(MDQ_ERR_INVALID_ARG, "tensor %d: null gradient", b + i);
+            c += chunks_of(n);  // <= 2^47 per tensor: no overflow across 256 tensors
+            if (c > INT32_MAX)
+                return mdq_fail(MDQ_ERR_TOO_LARGE, "too many elements in one call");
+        }
+        total += c;
+        if (total > INT32_MAX) return mdq_fail(MDQ_ERR_TOO_LARGE, "too many elements in one call");
+    }
+    *total_chunks = total;
+    return MDQ_OK;
+}
 
 }  // namespace
 
@@ -158,10 +187,8 @@ mdq_status mdq_grad_stats_workspace_bytes(const int64_t* counts, int32_t n_tenso
     if (n_tensors < 0 || (n_tensors > 0 && counts == nullptr) || bytes == nullptr)
         return mdq_fail(MDQ_ERR_INVALID_ARG, "bad arguments");
     int64_t chunks = 0;
-    for (int i = 0; i < n_tensors; ++i) {
-        if (counts[i] < 0) return mdq_fail(MDQ_ERR_INVALID_ARG, "tensor %d: negative count", i);
-        chunks += chunks_of(counts[i]);
-    }
+    const mdq_status st = validate_stats_call(nullptr, counts, n_tensors, &chunks);
+    if (st != MDQ_OK) return st;
     *bytes = chunks * 3 * (int64_t)sizeof(double);
     return MDQ_OK;
 }
@@ -175,9 +202,10 @@ mdq_status mdq_grad_stats_multi(const void* const* grads, const int64_t* counts,
         return mdq_fail(MDQ_ERR_INVALID_ARG, "null argument");
     if (grad_dtype != MDQ_F32 && grad_dtype != MDQ_BF16)
         return mdq_fail(MDQ_ERR_UNSUPPORTED, "grad dtype must be MDQ_F32 or MDQ_BF16");
-    int64_t need = 0;
-    mdq_status st = mdq_grad_stats_workspace_bytes(counts, n_tensors, &need);
+    int64_t chunks = 0;
+    mdq_status st = validate_stats_call(grads, counts, n_tensors, &chunks);
     if (st != MDQ_OK) return st;
+    const int64_t need = chunks * 3 * (int64_t)sizeof(double);
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))
         return mdq_fail(MDQ_ERR_INVALID_ARG, "workspace holds %lld bytes, %lld needed",
                     (long long)workspace_bytes, (long long)need);
@@ -188,14 +216,11 @@ mdq_status mdq_grad_stats_multi(const void* const* grads, const int64_t* counts,
         const int cnt = n_tensors - b < kCap ? n_tensors - b : kCap;
         P.n = cnt;
         int64_t c = 0;
-        for (int i = 0; i < cnt; ++i) {
-            if (counts[b + i] > 0 && grads[b + i] == nullptr)
-                return mdq_fail(MDQ_ERR_INVALID_ARG, "tensor %d: null gradient", b + i);
+        for (int i = 0; i < cnt; ++i) {  // (validated above)
             P.g[i] = grads[b + i];
             P.count[i] = counts[b + i];
             P.chunk_begin[i] = (int32_t)c;
             c += chunks_of(counts[b + i]);
-            if (c > INT32_MAX) return mdq_fail(MDQ_ERR_TOO_LARGE, "too many elements in one call");
         }
         P.chunk_begin[cnt] = (int32_t)c;
         P.total_chunks = (int32_t)c;
@@ -238,9 +263,44 @@ static __device__ __align__(256) double g_noalloc_partials[kNoAllocRecords * 3];
 
 // Device address of g_noalloc_partials per device.  The host-side name of the
 // array is only a stand-in; its device address comes from
-// cudaGetSymbolAddress, looked up once per device with that device current.
+// cudaGetSymbolAddress, looked up with that device current.  The address
+// belongs to the device's current context: it is cached together with that
+// context's unique id and looked up again when the id changes (for instance
+// after the caller reset the device, which destroys the context).
+typedef int (*CtxGetCurrentFn)(void** ctx);
+typedef int (*CtxGetIdFn)(void* ctx, unsigned long long* id);
+
+struct NoallocSlot {
+    void* addr;
+    unsigned long long ctx_id;
+};
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
+NoallocSlot g_noalloc_slot[64] = {};
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+bool g_ctx_fns_looked_up = false;
+
+// Unique id of the calling thread's current context, 0 when the driver cannot
+// tell (then the cached address is trusted as is).
+unsigned long long current_ctx_id() {
+    if (!g_ctx_fns_looked_up) {
+        g_ctx_fns_looked_up = true;
+        void* f1 = nullptr;
+        void* f2 = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) == cudaSuccess &&
+            cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) == cudaSuccess &&
+            q1 == cudaDriverEntryPointSuccess && q2 == cudaDriverEntryPointSuccess) {
+            g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+            g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
+        }
+    }
+    if (g_ctx_get_current == nullptr || g_ctx_get_id == nullptr) return 0;
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_get_current(&ctx) != 0 || ctx == nullptr || g_ctx_get_id(ctx, &id) != 0) return 0;
+    return id;
+}
 
 mdq_status noalloc_scratch(void** ptr) {
     int dev = 0;
@@ -248,14 +308,17 @@ mdq_status noalloc_scratch(void** ptr) {
     if (e != cudaSuccess) return mdq_fail(MDQ_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= 64) return mdq_fail(MDQ_ERR_CUDA, "device index %d out of range", dev);
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (g_noalloc_addr[dev] == nullptr) {
+    const unsigned long long id = current_ctx_id();
+    NoallocSlot& slot = g_noalloc_slot[dev];
+    if (slot.addr == nullptr || (id != 0 && id != slot.ctx_id)) {
         void* a = nullptr;
         e = cudaGetSymbolAddress(&a, g_noalloc_partials);
         if (e != cudaSuccess || a == nullptr)
             return mdq_fail(MDQ_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-        g_noalloc_addr[dev] = a;
+        slot.addr = a;
+        slot.ctx_id = current_ctx_id();  // the lookup may have created the context
     }
-    *ptr = g_noalloc_addr[dev];
+    *ptr = slot.addr;
     return MDQ_OK;
 }
 

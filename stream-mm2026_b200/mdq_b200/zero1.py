@@ -122,6 +122,7 @@ class ShardLayout:
                 a, e = max(off, lo), min(off + n, hi)
                 if a < e:
                     out.append(Piece(param=i, start=a - off, n=e - a, flat_off=a))
+        assert len({pc.param for pc in out}) == len(out), "one piece per parameter and rank"
         return out
 
 
@@ -288,9 +289,13 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         views = [self._piece_views(pc)[1] for pc in self.pieces]
         if views and self.flat_grad.is_cuda:
             # One fused pass over every local piece (mdq_grad_stats_multi).
+            # A rank holds at most one piece of each parameter (a parameter
+            # lies in one bucket, and a rank's shard of a bucket is one
+            # contiguous range), so the rows are copied, not summed: no
+            # order-dependent floating-point accumulation.
             part = kernels.grad_stats(views)
             idx = torch.tensor([pc.param for pc in self.pieces], device=sums.device)
-            sums.index_add_(0, idx, part)
+            sums.index_copy_(0, idx, part)
         else:
             # The same float64 sums with torch reductions (host tensors).
             for pc, g in zip(self.pieces, views):

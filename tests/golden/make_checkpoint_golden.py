@@ -33,6 +33,19 @@ KW = dict(lr=1e-3, weight_decay=0.01, layer_count=12, batch_size=16, update_freq
           block_size=256)
 
 
+
+def _reference_root(explicit):
+    """The reference checkout (see oracle/build_ref.py:reference_root)."""
+    repo = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    if repo not in sys.path:
+        sys.path.insert(0, repo)
+    from oracle.build_ref import reference_root
+
+    root = reference_root(explicit)
+    if root is None:
+        raise SystemExit("reference checkout not found: pass --reference or set MDQ_REFERENCE_ROOT")
+    return root
+
 def groups(params):
     half = (len(params) + 1) // 2
     return [{"params": params[:half]}, {"params": params[half:], "weight_decay": 0.0}]
@@ -61,8 +74,9 @@ def final_record(params, opt):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     a = ap.parse_args()
+    a.reference = _reference_root(a.reference)
     torch.set_num_threads(1)
     simple, fused = import_reference_classes(a.reference)
     for name, cls in (("simple", simple), ("fusedio", fused)):

@@ -1,7 +1,7 @@
 """Generate host-logic golden trajectories from the reference's optimizer classes.
 
-Run in a container that holds the reference checkout (default /root/reference;
-``--reference`` to change).  The reference classes
+Run in a container that holds the reference checkout (``--reference PATH``,
+else ``MDQ_REFERENCE_ROOT``, else BASELINE.json's ``reference_path``).  The reference classes
 (CUDA/stquant_opt_simple.py:MDQAdamWSimple, CUDA/stquant_opt_fused_io.py:
 MDQAdamWSimpleFusedIO) import the CUDA extension ``stquant_timetest_cpp`` at
 module top; here that module is provided by the CPU oracle
@@ -34,6 +34,19 @@ from oracle import oracle  # noqa: E402
 from host_scenario import SCENARIOS, run_scenario  # noqa: E402
 
 
+
+def _reference_root(explicit):
+    """The reference checkout (see oracle/build_ref.py:reference_root)."""
+    repo = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    if repo not in sys.path:
+        sys.path.insert(0, repo)
+    from oracle.build_ref import reference_root
+
+    root = reference_root(explicit)
+    if root is None:
+        raise SystemExit("reference checkout not found: pass --reference or set MDQ_REFERENCE_ROOT")
+    return root
+
 def import_reference_classes(reference_root: str):
     fake = types.ModuleType("stquant_timetest_cpp")
     fake.fused_mdq_adamw = oracle.fused_mdq_adamw_cpu
@@ -46,9 +59,10 @@ def import_reference_classes(reference_root: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     ap.add_argument("--out", default=os.path.join(HERE, "host_trajectories.npz"))
     a = ap.parse_args()
+    a.reference = _reference_root(a.reference)
     torch.set_num_threads(1)
     simple, fused = import_reference_classes(a.reference)
     classes = {"simple": simple, "fusedio": fused}

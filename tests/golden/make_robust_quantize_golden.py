@@ -1,7 +1,8 @@
 """Golden vectors for robust_quantize from the reference's pure-PyTorch
 optimizer (baseline/mdqbock_newhook.py:58-83, MDQAdamW.robust_quantize).
 
-Run where the reference checkout exists (default /root/reference):
+Run where the reference checkout exists (``--reference PATH``, else
+``MDQ_REFERENCE_ROOT``, else BASELINE.json's ``reference_path``):
 
     python tests/golden/make_robust_quantize_golden.py [--reference PATH]
 
@@ -19,11 +20,25 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
+
+def _reference_root(explicit):
+    """The reference checkout (see oracle/build_ref.py:reference_root)."""
+    repo = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    if repo not in sys.path:
+        sys.path.insert(0, repo)
+    from oracle.build_ref import reference_root
+
+    root = reference_root(explicit)
+    if root is None:
+        raise SystemExit("reference checkout not found: pass --reference or set MDQ_REFERENCE_ROOT")
+    return root
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     ap.add_argument("--out", default=os.path.join(HERE, "robust_quantize.npz"))
     a = ap.parse_args()
+    a.reference = _reference_root(a.reference)
     sys.path.insert(0, os.path.join(a.reference, "baseline"))
     from mdqbock_newhook import MDQAdamW  # noqa: E402
 

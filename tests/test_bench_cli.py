@@ -1,5 +1,8 @@
 """bench.py's reference arm runs on CPU and keeps the JSON contract, for both
-code widths (the arm times the CPU restatement of the reference kernel)."""
+code widths.  The arm times the reference's own pure-PyTorch optimizer
+(baseline/mdqbock_newhook.py, byte-compiled into oracle/_ref by the build) and
+falls back to the C restatement of the reference kernel when that module was
+not built."""
 import json
 import os
 import subprocess
@@ -19,7 +22,11 @@ def test_reference_arm_json_line(bits):
     assert line["impl"] == "reference" and line["unit"] == "Gparams/s"
     assert line["value"] > 0 and line["higher_is_better"] is True
     assert line["config"]["bits"] == bits
-    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    base = line["cpu_baseline"]
+    ref_built = os.path.isfile(os.path.join(REPO, "oracle", "_ref", "mdqbock_newhook.pyc"))
+    assert base["kind"] == ("reference" if ref_built else "port") and base["cores"] >= 1
+    if ref_built:
+        assert "mdqbock_newhook" in base["sample"] and "8]-bit" in base["sample"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
 
 

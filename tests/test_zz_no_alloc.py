@@ -49,13 +49,17 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device, dtype):
 
 
 def test_noalloc_refuses_calls_beyond_its_scratch(cuda_device):
+    """65537 one-element tensors need 65537 partial records, one more than the
+    built-in scratch holds.  Every pointer is a real element of one buffer, so
+    even a broken size guard would only read valid memory."""
     lib = _lib.load()
-    g = torch.zeros(8, device=cuda_device)
-    n = 2
-    ptrs = (ctypes.c_void_p * n)(g.data_ptr(), g.data_ptr())
-    # 2 x (2^31 + 1) elements need 2 x 32769 records: over the built-in 65536.
-    counts = (ctypes.c_int64 * n)((1 << 31) + 1, (1 << 31) + 1)
-    out = torch.empty(n, 4, dtype=torch.float64, device=cuda_device)
+    n = 65537
+    g = torch.zeros(n, device=cuda_device)
+    ptrs = (ctypes.c_void_p * n)(*[g.data_ptr() + 4 * i for i in range(n)])
+    counts = (ctypes.c_int64 * n)(*([1] * n))
+    out = torch.full((n, 4), 7.0, dtype=torch.float64, device=cuda_device)
     st = lib.mdq_grad_stats_multi_noalloc(ptrs, counts, n, _lib.MDQ_F32, out.data_ptr(), None)
+    torch.cuda.synchronize()
     assert st == _lib.MDQ_ERR_TOO_LARGE
     assert "scratch holds 65536" in lib.mdq_last_error().decode()
+    assert bool((out == 7.0).all()), "a refused call must not write its output"
