@@ -380,11 +380,12 @@ def reference_cpu_baseline(budget_s=12.0, min_steps=20):
     and reports the median step.  None when the reference module is absent."""
     import torch
 
-    if not os.path.isfile(os.path.join(REF_DIR, "mdqbock_newhook.pyc")):
+    from oracle import build_ref
+
+    try:
+        MDQAdamW = build_ref.load_python_module("mdqbock_newhook").MDQAdamW  # unmodified
+    except FileNotFoundError:
         return None
-    if REF_DIR not in sys.path:
-        sys.path.insert(0, REF_DIR)
-    from mdqbock_newhook import MDQAdamW  # the reference's class, unmodified
 
     cores = host_cores()
     torch.set_num_threads(cores)

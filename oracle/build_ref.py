@@ -21,10 +21,12 @@ against the reference's own arithmetic, CUDA libm included.
 The reference's pure-PyTorch optimizer (``baseline/mdqbock_newhook.py``) and
 its two CUDA optimizer classes (``CUDA/stquant_opt_simple.py``,
 ``CUDA/stquant_opt_fused_io.py``) are byte-compiled the same way: each is
-compiled where it lies into a sourceless ``oracle/_ref/<module>.pyc`` (same
-interpreter as the GPU box), so the GPU box, which has no reference checkout,
-can import and run the reference's own unmodified classes beside ours (the
-timed CPU baseline of ``bench.py --impl reference`` and the GPU parity tests).
+compiled where it lies into sourceless bytecode ``oracle/_ref/<module>.pycode``
+(same interpreter as the GPU box; the suffix is not ``.pyc`` so that tools
+which drop Python caches keep it), so the GPU box, which has no reference
+checkout, can load and run the reference's own unmodified classes beside ours
+(the timed CPU baseline of ``bench.py --impl reference`` and the GPU parity
+tests) with ``load_python_module``.
 
 The checkout is found from ``--reference``, else ``MDQ_REFERENCE_ROOT``, else
 the ``reference_path`` that ``BASELINE.json`` records.
@@ -66,8 +68,41 @@ def reference_root(explicit: str | None = None) -> str | None:
     return None
 
 
+BYTECODE_SUFFIX = ".pycode"
+
+
 def python_modules_built() -> bool:
-    return all(os.path.isfile(os.path.join(OUT_DIR, m + ".pyc")) for m, _ in PY_MODULES)
+    return all(os.path.isfile(os.path.join(OUT_DIR, m + BYTECODE_SUFFIX)) for m, _ in PY_MODULES)
+
+
+def load_python_module(name: str, extra_modules: dict | None = None):
+    """Load the reference module `name` from its bytecode in oracle/_ref and
+    return it (registered in sys.modules under `name`).  `extra_modules`
+    (name -> module) are visible in sys.modules while it executes, so its own
+    imports resolve to the reference's files; they are removed afterwards
+    unless they were there before."""
+    import importlib.machinery
+    import importlib.util
+
+    path = os.path.join(OUT_DIR, name + BYTECODE_SUFFIX)
+    if not os.path.isfile(path):
+        raise FileNotFoundError(f"{path}: run python oracle/build_ref.py")
+    extra = dict(extra_modules or {})
+    saved = {k: sys.modules.get(k) for k in extra}
+    try:
+        sys.modules.update(extra)
+        loader = importlib.machinery.SourcelessFileLoader(name, path)
+        spec = importlib.util.spec_from_file_location(name, path, loader=loader)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        loader.exec_module(mod)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+    return mod
 
 
 def stage_python(reference_root: str) -> list[str]:
@@ -76,7 +111,7 @@ def stage_python(reference_root: str) -> list[str]:
     out = []
     for mod, rel in PY_MODULES:
         src = os.path.join(reference_root, rel)
-        dst = os.path.join(OUT_DIR, mod + ".pyc")
+        dst = os.path.join(OUT_DIR, mod + BYTECODE_SUFFIX)
         py_compile.compile(src, cfile=dst, doraise=True,
                            invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
         out.append(dst)

@@ -45,7 +45,7 @@ import torch.distributed as dist
 
 from . import kernels
 from ._lib import TensorDesc
-from .optim import MDQAdamWSimpleFusedIO, _zero_codes
+from .optim import MDQAdamWSimpleFusedIO, _zero_codes, stats_from_sums
 
 
 @dataclass
@@ -306,12 +306,7 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
                 sums[pc.param, 3] += pc.n
         if self.world > 1:
             dist.all_reduce(sums, group=self.group)
-        s, s2, sa, cnt = sums.unbind(1)
-        mean_sq = s2 / cnt
-        var = (s2 - s * s / cnt) / (cnt - 1)
-        n_l = torch.sqrt(mean_sq)
-        r_l = torch.sqrt(var.clamp_min(0)) / (sa / cnt + 1e-12)
-        return torch.stack([n_l, r_l, mean_sq], 1).float()
+        return stats_from_sums(sums)
 
     def _decide_bits_sharded(self):
         stats = self._global_grad_stats()

@@ -8,6 +8,8 @@ from __future__ import annotations
 
 import glob
 import importlib
+import importlib.machinery
+import importlib.util
 import os
 import sys
 
@@ -25,13 +27,51 @@ CODE_DTYPES = {
 }
 
 
+_REF_EXT = None
+_REF_CLASSES = None
+
+
 def load_reference_kernel():
-    """Import the reference's compiled extension from oracle/_ref (GPU box)."""
-    if not glob.glob(os.path.join(REF_DIR, "stquant_timetest_cpp*.so")):
-        raise RuntimeError("oracle/_ref has no reference build; run python oracle/build_ref.py")
-    if REF_DIR not in sys.path:
-        sys.path.insert(0, REF_DIR)
-    return importlib.import_module("stquant_timetest_cpp")
+    """The reference's compiled extension from oracle/_ref (GPU box), loaded
+    from its file under its own module name (this repository's drop-in shim
+    of the same name, stream-mm2026_b200/stquant_timetest_cpp.py, may be on
+    sys.path too; it is never what this returns)."""
+    global _REF_EXT
+    if _REF_EXT is None:
+        found = glob.glob(os.path.join(REF_DIR, "stquant_timetest_cpp*.so"))
+        if not found:
+            raise RuntimeError("oracle/_ref has no reference build; run python oracle/build_ref.py")
+        import torch  # noqa: F401  (the extension links against torch)
+
+        loader = importlib.machinery.ExtensionFileLoader("stquant_timetest_cpp", found[0])
+        spec = importlib.util.spec_from_file_location("stquant_timetest_cpp", found[0],
+                                                      loader=loader)
+        mod = importlib.util.module_from_spec(spec)
+        loader.exec_module(mod)
+        _REF_EXT = mod
+    return _REF_EXT
+
+
+def load_reference_classes():
+    """The reference's own optimizer classes, unmodified
+    (CUDA/stquant_opt_simple.py:MDQAdamWSimple and
+    CUDA/stquant_opt_fused_io.py:MDQAdamWSimpleFusedIO, byte-compiled into
+    oracle/_ref by oracle/build_ref.py), bound to the reference's own compiled
+    kernel.  Returns (MDQAdamWSimple, MDQAdamWSimpleFusedIO)."""
+    global _REF_CLASSES
+    if _REF_CLASSES is None:
+        from oracle import build_ref
+
+        ext = load_reference_kernel()
+        simple = build_ref.load_python_module("stquant_opt_simple",
+                                              {"stquant_timetest_cpp": ext})
+        fused = build_ref.load_python_module("stquant_opt_fused_io",
+                                             {"stquant_timetest_cpp": ext,
+                                              "stquant_opt_simple": simple})
+        for name in ("stquant_opt_simple", "stquant_opt_fused_io"):
+            sys.modules.pop(name, None)
+        _REF_CLASSES = (simple.MDQAdamWSimple, fused.MDQAdamWSimpleFusedIO)
+    return _REF_CLASSES
 
 
 class State:

@@ -23,7 +23,7 @@ def test_reference_arm_json_line(bits):
     assert line["value"] > 0 and line["higher_is_better"] is True
     assert line["config"]["bits"] == bits
     base = line["cpu_baseline"]
-    ref_built = os.path.isfile(os.path.join(REPO, "oracle", "_ref", "mdqbock_newhook.pyc"))
+    ref_built = os.path.isfile(os.path.join(REPO, "oracle", "_ref", "mdqbock_newhook.pycode"))
     assert base["kind"] == ("reference" if ref_built else "port") and base["cores"] >= 1
     if ref_built:
         assert "mdqbock_newhook" in base["sample"] and "8]-bit" in base["sample"]

@@ -33,9 +33,24 @@ def oracle_launch(self, items, device):
                     it.eps, it.step, it.m_bits, it.v_bits)
 
 
+def cpu_fused_stats(self, params_with_grad):
+    """Test double of the fused statistics pass for CPU tensors: the same
+    float64 (sum g, sum g^2, sum |g|, count) rows, then stats_from_sums."""
+    rows = []
+    for p, _ in params_with_grad:
+        g = p.grad.double().reshape(-1)
+        rows.append(torch.stack([g.sum(), (g * g).sum(), g.abs().sum(),
+                                 torch.tensor(float(g.numel()), dtype=torch.float64)]))
+    return list(optim.stats_from_sums(torch.stack(rows)))
+
+
 @pytest.fixture
 def cpu_kernel(monkeypatch):
     monkeypatch.setattr(optim.MDQAdamWSimple, "_launch", oracle_launch)
+    # CPU tensors: the policy statistics come from the reference's own torch
+    # reductions (the fused statistics pass is a CUDA kernel).
+    monkeypatch.setattr(optim.MDQAdamWSimple, "_grad_stats_all",
+                        lambda self, pwg: [self._compute_grad_stats(p.grad) for p, _ in pwg])
     torch.set_num_threads(1)
 
 

@@ -34,6 +34,10 @@ def test_robust_quantize_matches_reference():
 @pytest.fixture
 def cpu_kernel(monkeypatch):
     monkeypatch.setattr(optim.MDQAdamWSimple, "_launch", oracle_launch)
+    # CPU tensors: the policy statistics come from the reference's own torch
+    # reductions (the fused statistics pass is a CUDA kernel).
+    monkeypatch.setattr(optim.MDQAdamWSimple, "_grad_stats_all",
+                        lambda self, pwg: [self._compute_grad_stats(p.grad) for p, _ in pwg])
     torch.set_num_threads(1)
 
 

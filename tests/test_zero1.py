@@ -43,6 +43,7 @@ def _use_oracle():
     from mdq_b200 import optim
 
     optim.MDQAdamWSimple._launch = test_host_parity.oracle_launch
+    optim.MDQAdamWSimple._grad_stats_all = test_host_parity.cpu_fused_stats
 
 
 def _unsharded(world, steps, kw, sizes):
