@@ -299,46 +299,226 @@ def gpt2_medium_shapes():
     return shapes
 
 
-def run_zero1(args, rank, world, device):
-    """ZeRO-1 step on N GPUs (BASELINE config 4 shapes and precision): bf16
-    gradients reduce-scattered over NCCL, the fused 8-bit-m / 4-bit-v step on
-    each rank's shard, fp32 parameters all-gathered in place.  Device time of
-    the whole optimizer.step(), max over ranks."""
+def llama7b_shapes():
+    """Parameter shapes of LLaMA-7B (32 layers, d=4096, 32 heads, SwiGLU FFN
+    11008, RMSNorm, vocab 32000, untied embedding and head): 6.74B parameters."""
+    d, f, v, layers = 4096, 11008, 32000, 32
+    shapes = [(v, d)]
+    for _ in range(layers):
+        shapes += [(d,), (d, d), (d, d), (d, d), (d, d), (d,), (f, d), (f, d), (d, f)]
+    shapes += [(d,), (v, d)]
+    return shapes
+
+
+SHARDED_MODELS = {
+    # BASELINE config 4: GPT-2 medium, 8-bit m / 4-bit v
+    "gpt2-medium": dict(shapes=gpt2_medium_shapes, bits=(8, 4), block=256),
+    # BASELINE config 5: LLaMA-7B, 4-bit m / v (block 256 as the reference's
+    # 7B driver, CUDA/7B/llama7b_common.py:190-197)
+    "llama-7b": dict(shapes=llama7b_shapes, bits=4, block=256),
+}
+
+
+def _max_over_ranks(x, device, world):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return x
+    t = torch.tensor(x, device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems):
+    """One ZeroMDQAdamW.step() of a fixed model on N GPUs (strong scaling:
+    the model is the same at every N): bf16 gradients reduce-scattered over
+    NCCL, the fused step on each rank's shard, parameters all-gathered.  The
+    gradients are synthetic (written into the flat gradient buffer, as
+    backward would leave them).  Device times, max over ranks; the phases
+    come from CUDA events inside step() (profile_phases)."""
     import torch
     import torch.distributed as dist
 
     from mdq_b200.zero1 import ZeroMDQAdamW
 
-    g = torch.Generator(device=device).manual_seed(rank)
-    params = [torch.nn.Parameter(torch.randn(sh, device=device, generator=g) * 0.02)
-              for sh in gpt2_medium_shapes()]
+    spec = SHARDED_MODELS[name]
+    g = torch.Generator(device=device).manual_seed(1234)
+    params = [torch.nn.Parameter(torch.empty(sh, device=device).normal_(0, 0.02, generator=g))
+              for sh in spec["shapes"]()]
     n = sum(p.numel() for p in params)
-    opt = ZeroMDQAdamW(params, lr=1e-3, weight_decay=0.01, block_size=256, fixed_bits=(8, 4),
-                       p_mode="fast", grad_dtype=torch.bfloat16)
-    opt.flat_grad.normal_(0, 1e-3, generator=g)
+    opt = ZeroMDQAdamW(params, lr=1e-3, weight_decay=0.01, block_size=spec["block"],
+                       fixed_bits=spec["bits"], p_mode="fast", grad_dtype=torch.bfloat16,
+                       param_dtype=param_dtype, bucket_elems=bucket_elems, profile_phases=True)
+    del params
+    opt.flat_grad.normal_(0, 1e-3, generator=torch.Generator(device=device).manual_seed(rank))
     for _ in range(3):
         opt.step()
     torch.cuda.synchronize()
-    dist.barrier()
-    steps = max(5, min(args.steps, 20))
+    if world > 1:
+        dist.barrier()
+    steps = max(5, min(args.steps, 10))
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    phases = []
     a.record()
     for _ in range(steps):
         opt.step()
+        phases.append(opt._phase_events)
     b.record()
     torch.cuda.synchronize()
-    x = torch.tensor([a.elapsed_time(b) / steps], device=device)
-    dist.all_reduce(x, op=dist.ReduceOp.MAX)
-    ms = float(x.item())
+    total_ms = a.elapsed_time(b) / steps
+    ph = {k: 0.0 for k in ("reduce_scatter", "step", "all_gather_tail")}
+    for ev in phases:
+        e0, e1, e2, e3 = ev
+        ph["reduce_scatter"] += e0.elapsed_time(e1) / steps
+        ph["step"] += e1.elapsed_time(e2) / steps
+        ph["all_gather_tail"] += e2.elapsed_time(e3) / steps
+    vals = _max_over_ranks([total_ms, ph["reduce_scatter"], ph["step"], ph["all_gather_tail"]],
+                           device, world)
+    total_ms, rs_ms, step_ms, ag_ms = vals
     total = opt.layout.total
-    link_bytes = (world - 1) * total // world * (2 + 4)   # RS of bf16 + AG of fp32, per GPU out
-    return {"model": "gpt2-medium shapes (355M params)", "params": n, "m_bits": 8, "v_bits": 4,
-            "block": 256, "grad_dtype": "bf16", "ms_per_step": round(ms, 3),
-            "gparams_per_s": round(n / (ms * 1e-3) / 1e9, 2),
-            "nvlink_bytes_per_gpu_per_step": link_bytes,
-            "nvlink_gbs_per_gpu": round(link_bytes / (ms * 1e-3) / 1e9, 1),
-            "what": "optimizer.step(): reduce-scatter(avg) bf16 grads + fused step on the "
-                    "shard + all-gather fp32 params (NCCL), device time, max over ranks"}
+    pbytes = 4 if param_dtype == torch.float32 else 2
+    rs_bytes = (world - 1) * total // world * 2            # bf16 grads, per GPU
+    ag_bytes = (world - 1) * total // world * pbytes
+    out = {"model": f"{name} shapes ({n / 1e9:.3f}B params)", "params": n,
+           "bits": spec["bits"], "block": spec["block"], "grad_dtype": "bf16",
+           "param_dtype": "fp32" if param_dtype == torch.float32 else "bf16 (fp32 master shard)",
+           "buckets": len(opt.layout.buckets), "steps": steps,
+           "ms_per_step": round(total_ms, 3),
+           "gparams_per_s": round(n / (total_ms * 1e-3) / 1e9, 2),
+           "phases_ms": {"reduce_scatter": round(rs_ms, 3), "step": round(step_ms, 3),
+                         "all_gather_tail": round(ag_ms, 3)},
+           "step_only_gparams_per_s": round(n / (step_ms * 1e-3) / 1e9, 2)}
+    if world > 1:
+        out["nvlink"] = {
+            "rs_bytes_per_gpu": rs_bytes, "ag_bytes_per_gpu": ag_bytes,
+            "rs_busbw_gbs": round(rs_bytes / (rs_ms * 1e-3) / 1e9, 1) if rs_ms > 0 else None,
+            "ag_busbw_gbs": (round(ag_bytes / (ag_ms * 1e-3) / 1e9, 1)
+                             if len(opt.layout.buckets) == 1 and ag_ms > 0 else None)}
+    del opt
+    torch.cuda.empty_cache()
+    return out
+
+
+def nccl_busbw(world, device, nbytes=1 << 30):
+    """Bus bandwidth of a plain NCCL all-gather and reduce-scatter of `nbytes`
+    (bf16) in this run, the yardstick for the sharded step's collectives."""
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return None
+    n = nbytes // 2
+    full = torch.empty(n, dtype=torch.bfloat16, device=device)
+    shard = full[: n // world]
+    res = {}
+    for name in ("all_gather", "reduce_scatter"):
+        def op():
+            if name == "all_gather":
+                dist.all_gather_into_tensor(full, shard)
+            else:
+                dist.reduce_scatter_tensor(shard, full, op=dist.ReduceOp.AVG)
+        for _ in range(3):
+            op()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            op()
+        b.record()
+        torch.cuda.synchronize()
+        ms = _max_over_ranks([a.elapsed_time(b) / 10], device, world)[0]
+        res[name + "_busbw_gbs"] = round((world - 1) / world * nbytes / (ms * 1e-3) / 1e9, 1)
+    res["bytes"] = nbytes
+    del full
+    torch.cuda.empty_cache()
+    return res
+
+
+def zero1_parity(world, rank, device):
+    """Sharded == unsharded, checked inside the bench run: a small model
+    (awkward sizes, a parameter spanning ranks) stepped 5 times by
+    ZeroMDQAdamW over NCCL and, on every rank, by the unsharded
+    MDQAdamWSimpleFusedIO on the averaged gradients.  Gradients are small
+    multiples of 2^-20, so the average over a power-of-two world is exact.
+    Parameters, codes, scales and step counters of every local piece must be
+    identical, for fixed 4-bit, fixed (8, 4) and the score policy, exact p,
+    fp32 parameters; and for bf16 parameters (fp32 master) the master must
+    equal the unsharded parameters and the gathered bf16 parameters their
+    rounding.  Returns True only if every rank agrees."""
+    import torch
+    import torch.distributed as dist
+
+    from mdq_b200.optim import MDQAdamWSimpleFusedIO
+    from mdq_b200.zero1 import ZeroMDQAdamW
+
+    sizes = [1000, 3, (1 << 20) + 17, 256, 777, 2048, 5, 65536 * 3 + 5]
+
+    def grads(r, t, bf16):
+        gg = torch.Generator().manual_seed(1000 * t + r)
+        if bf16:
+            # |k| <= 15 units of 2^-12: every partial sum of up to 8 ranks is
+            # exact in bfloat16, whatever order the reduction takes.
+            return [torch.round(torch.randn(n, generator=gg) * 4).clamp(-15, 15) / 2 ** 12
+                    for n in sizes]
+        return [(torch.round(torch.randn(n, generator=gg) * 1024 * 2.0 ** (i % 3)) / 2 ** 20)
+                for i, n in enumerate(sizes)]
+
+    def params():
+        gg = torch.Generator().manual_seed(0)
+        return [torch.nn.Parameter((torch.randn(n, generator=gg) * 0.02).to(device))
+                for n in sizes]
+
+    ok = True
+    for kw, pdt in ((dict(fixed_bits=4), torch.float32), (dict(fixed_bits=(8, 4)), torch.float32),
+                    (dict(), torch.float32), (dict(fixed_bits=4), torch.bfloat16)):
+        common = dict(lr=1e-3, weight_decay=0.01, block_size=256, p_mode="exact", **kw)
+        ref = params()
+        ref_opt = MDQAdamWSimpleFusedIO(ref, **common)
+        mine = params()
+        opt = ZeroMDQAdamW(mine, bucket_elems=400_000, param_dtype=pdt,
+                           grad_dtype=torch.bfloat16 if pdt == torch.bfloat16 else torch.float32,
+                           **common)
+        for t in range(1, 6):
+            per = [grads(r, t, pdt == torch.bfloat16) for r in range(world)]
+            opt.zero_grad()
+            for i, p in enumerate(ref):
+                avg = sum(pr[i] for pr in per) / world
+                p.grad = avg.to(device)
+                mine[i].grad.copy_(per[rank][i].to(mine[i].grad.dtype))
+            ref_opt.step()
+            opt.step()
+        torch.cuda.synchronize()
+        master = opt.master_params()
+        for i, p in enumerate(ref):
+            rs, st = ref_opt.state[p], opt.state[mine[i]]
+            ok &= int(rs["step"]) == int(st["step"])
+            if pdt == torch.float32:
+                ok &= torch.equal(p.detach().view(torch.int32), mine[i].detach().view(torch.int32))
+            else:
+                ok &= torch.equal(p.detach().to(torch.bfloat16).view(torch.int16),
+                                  mine[i].detach().view(torch.int16))
+            if i not in master:
+                continue
+            start, mp = master[i]
+            pc_n = mp.numel()
+            ok &= torch.equal(p.detach().reshape(-1)[start:start + pc_n].view(torch.int32),
+                              mp.view(torch.int32))
+            b0, nb = start // 256, -(-pc_n // 256)
+            for k in ("scale_m", "scale_v", "v_min"):
+                ok &= torch.equal(rs[k][b0:b0 + nb].view(torch.int32), st[k].view(torch.int32))
+            ea_r, ea = rs["exp_avg"], st["exp_avg"]
+            ok &= torch.equal(ea_r.reshape(-1)[start:start + pc_n], ea)
+            if rs["exp_avg_sq"].numel() == rs["exp_avg"].numel():
+                ok &= torch.equal(rs["exp_avg_sq"].reshape(-1)[start:start + pc_n],
+                                  st["exp_avg_sq"])
+            elif rs["exp_avg_sq"].numel():
+                ok &= torch.equal(rs["exp_avg_sq"][start // 2:start // 2 + (pc_n + 1) // 2],
+                                  st["exp_avg_sq"])
+        del opt, ref_opt
+    flag = torch.tensor([1 if ok else 0], device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
 
 
 def traffic_per_launch(n_elems):
@@ -490,6 +670,8 @@ def main() -> int:
     ap.add_argument("--impl", default="mdq_b200", choices=["mdq_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the ZeRO-1 runs of the GPT-2-medium / LLaMA-7B shapes")
     ap.add_argument("--log2-elements", type=int, default=30,
                     help="elements per GPU = 2^k (profiling cases use smaller k)")
     ap.add_argument("--block", type=int, default=2048,
@@ -518,7 +700,21 @@ def main() -> int:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     ms, ms_exact, clocks, e2e = run_ours(args, rank, world, local_rank)
-    zero1 = run_zero1(args, rank, world, torch.device("cuda", local_rank)) if world > 1 else None
+    dev = torch.device("cuda", local_rank)
+    zero1 = None
+    if not args.no_sharded:
+        zero1 = {"what": "ZeroMDQAdamW.step() of fixed models (strong scaling): reduce-scatter "
+                         "(avg) of bf16 gradients, fused step on each rank's shard, all-gather of "
+                         "the parameters; device time, max over ranks",
+                 "runs": []}
+        for name in ("gpt2-medium", "llama-7b"):
+            zero1["runs"].append(run_sharded(args, rank, world, dev, name, torch.float32, None))
+            if world > 1:
+                zero1["runs"].append(run_sharded(args, rank, world, dev, name, torch.bfloat16,
+                                                 1 << 28))
+        zero1["nccl_reference"] = nccl_busbw(world, dev)
+        if world > 1:
+            zero1["zero1_parity"] = zero1_parity(world, rank, dev)
     n = 1 << LOG2_N
     value = world * n / (ms * 1e-3) / 1e9
     bytes_launch = n * BYTES_PER_ELEM
@@ -544,6 +740,8 @@ def main() -> int:
         }
         if zero1 is not None:
             line["zero1"] = zero1
+            if "zero1_parity" in zero1:
+                line["zero1_parity"] = zero1["zero1_parity"]
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

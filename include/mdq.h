@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define MDQ_ABI_VERSION 1
+#define MDQ_ABI_VERSION 2
 
 typedef enum mdq_status {
     MDQ_OK = 0,
@@ -100,6 +100,11 @@ typedef struct mdq_tensor_desc {
     int32_t v_bits;        /* 1..32, at most the v storage width               */
     int32_t layout;        /* mdq_layout                                       */
     int32_t grad_dtype;    /* MDQ_F32 or MDQ_BF16                              */
+    void* p_bf16;          /* NULL, or bf16 [n]: the updated parameters rounded
+                              to bfloat16 (round to nearest even) are also
+                              written here.  No reference counterpart: the
+                              step writes a sharded optimizer's bf16
+                              all-gather send buffer itself (ABI version 2)  */
 } mdq_tensor_desc;
 
 typedef struct mdq_step_options {

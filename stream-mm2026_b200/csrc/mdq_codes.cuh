@@ -51,6 +51,7 @@ struct TensorPtrs {
     float* sm;
     float* sv;
     float* vmin;
+    __nv_bfloat16* p16;  // optional bf16 copy of the updated parameters
 };
 
 template <int LAYOUT> struct Codes;

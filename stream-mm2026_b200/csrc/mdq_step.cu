@@ -30,6 +30,7 @@
 #include <stdio.h>
 #include <stdarg.h>
 #include <math.h>
+#include <stddef.h>
 #include <algorithm>
 #include <mutex>
 
@@ -38,6 +39,11 @@
 #include "mdq_codes.cuh"
 
 #include "mdq_tiles.cuh"
+
+// The C layout the Python mirror (mdq_b200/kernels.py, _lib.py) packs.
+static_assert(offsetof(mdq_tensor_desc, grad_dtype) == 104, "mdq_tensor_desc layout");
+static_assert(offsetof(mdq_tensor_desc, p_bf16) == 112, "mdq_tensor_desc layout");
+static_assert(sizeof(mdq_tensor_desc) == 120, "mdq_tensor_desc layout");
 
 namespace mdq {
 
@@ -117,7 +123,11 @@ __global__ void mdq_step_tree(const LaunchDesc D, unsigned long long* prof) {
         }
     }
     if (prof && tid == 0) prof_mark(pc, 3, t0);
-    if (ok) D.t.p[i] = update_p<EXACT_P>(D.t.p[i], m, v, C);
+    if (ok) {
+        const float pn = update_p<EXACT_P>(D.t.p[i], m, v, C);
+        D.t.p[i] = pn;
+        if (D.t.p16 != nullptr) D.t.p16[i] = __float2bfloat16_rn(pn);
+    }
     if (prof && tid == 0) {
         prof_mark(pc, 4, t0);
         for (int k = 0; k < kProfSlots; ++k) atomicAdd(prof + k, pc[k]);
@@ -180,6 +190,7 @@ bool aligned(const void* ptr, uintptr_t a) { return ((uintptr_t)ptr & (a - 1)) =
 
 bool vec_ok(const mdq_tensor_desc& d) {
     if (!aligned(d.p, 16)) return false;
+    if (d.p_bf16 != nullptr && !aligned(d.p_bf16, 8)) return false;
     if (!aligned(d.grad, 16)) return false;
     switch (d.layout) {
         case MDQ_LAYOUT_PACKED4: return aligned(d.exp_avg, 8);
@@ -240,6 +251,7 @@ mdq::LaunchDesc to_launch(const mdq_tensor_desc& d) {
     L.t.sm = d.scale_m;
     L.t.sv = d.scale_v;
     L.t.vmin = d.v_min;
+    L.t.p16 = static_cast<__nv_bfloat16*>(d.p_bf16);
     L.n = d.n;
     L.tile_begin = 0;
     L.step = d.step;

@@ -304,6 +304,26 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                 if (j < cnt[i]) T.p[e + j] = p[4 * i + j];
         }
     }
+    if (T.p16 != nullptr) {
+        // bf16 copy of the updated parameters (a sharded optimizer's
+        // all-gather send buffer), round to nearest even.
+#pragma unroll
+        for (int i = 0; i < NCH; ++i) {
+            const int64_t e = e_first + (int64_t)cstride * i;
+            if (FULL) {
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(p[4 * i + 0], p[4 * i + 1]);
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(p[4 * i + 2], p[4 * i + 3]);
+                uint2 w;
+                w.x = *reinterpret_cast<const unsigned*>(&lo);
+                w.y = *reinterpret_cast<const unsigned*>(&hi);
+                __stcs(reinterpret_cast<uint2*>(T.p16 + e), w);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < cnt[i]) T.p16[e + j] = __float2bfloat16_rn(p[4 * i + j]);
+            }
+        }
+    }
     if (PROF && tid == 0) prof_mark(pc, 4, t0);
 
     // ---- block statistics (CUDA/stquant_kernel.cu:184-199) -------------

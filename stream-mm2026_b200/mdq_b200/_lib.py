@@ -27,7 +27,7 @@ LAYOUT_PACKED4, LAYOUT_S8U8, LAYOUT_S16U16, LAYOUT_S32U32, LAYOUT_M8V4 = range(5
 # mdq_p_mode
 P_FAST, P_EXACT = 0, 1
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class TensorDesc(ctypes.Structure):
@@ -53,6 +53,7 @@ class TensorDesc(ctypes.Structure):
         ("v_bits", ctypes.c_int32),
         ("layout", ctypes.c_int32),
         ("grad_dtype", ctypes.c_int32),
+        ("p_bf16", ctypes.c_void_p),
     ]
 
 

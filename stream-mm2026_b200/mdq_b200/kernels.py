@@ -118,13 +118,14 @@ class StepItem:
     m_bits: int
     v_bits: int
     layout: int
+    p_bf16: Optional[torch.Tensor] = None   # bf16 copy of the updated parameters
 
 
 # mdq_tensor_desc as packed bytes: 7 pointers, int64 n, int32 step / block,
-# 5 floats, 4 int32 (no interior padding; tests/test_abi.py checks the
-# offsets against the ctypes mirror).  One pack_into per descriptor costs
+# 5 floats, 4 int32, 4 bytes of padding, one pointer (tests/test_abi.py
+# checks the offsets against the ctypes mirror).  One pack_into per descriptor costs
 # far less host time than 19 ctypes attribute stores.
-_DESC_FMT = struct.Struct("=7Qq2i5f4i")
+_DESC_FMT = struct.Struct("=7Qq2i5f4i4xQ")
 
 
 def fill_desc(d: TensorDesc, it: StepItem) -> None:
@@ -135,7 +136,8 @@ def fill_desc(d: TensorDesc, it: StepItem) -> None:
         it.scale_m.data_ptr(), it.scale_v.data_ptr(), it.v_min.data_ptr(),
         it.p.numel(), int(it.step), int(it.block), float(it.lr), float(it.weight_decay),
         float(it.eps), float(it.beta1), float(it.beta2), int(it.m_bits), int(it.v_bits),
-        int(it.layout), _DTYPE_CODE.get(it.grad.dtype, -1))
+        int(it.layout), _DTYPE_CODE.get(it.grad.dtype, -1),
+        it.p_bf16.data_ptr() if it.p_bf16 is not None else 0)
 
 
 def run_descs(descs, count: int, device: torch.device, p_mode: int = P_FAST,
@@ -162,6 +164,11 @@ def step_multi(items: Sequence[StepItem], p_mode: int = P_FAST,
             _need_contig(t, "step tensors")
             if t.device != dev:
                 raise RuntimeError("all tensors of one step_multi call must share a device")
+        if it.p_bf16 is not None:
+            _need_cuda(it.p_bf16, "p_bf16")
+            _need_contig(it.p_bf16, "p_bf16")
+            if it.p_bf16.dtype != torch.bfloat16 or it.p_bf16.numel() != it.p.numel():
+                raise RuntimeError("p_bf16 must be a bfloat16 tensor of p's size")
         fill_desc(d, it)
     run_descs(arr, len(items), dev, p_mode, profile_cycles)
 

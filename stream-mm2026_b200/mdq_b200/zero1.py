@@ -139,12 +139,31 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
     ``no_sync()`` (gradient accumulation) the hooks launch nothing.  The block
     is one per optimizer (``block_size``, clamped to 1024 unless
     ``exact_block``).
+
+    ``param_dtype`` is the dtype of the model's parameters and of the
+    all-gather.  float32 (default) is the reference's: the fused step updates
+    the rank's shard of the fp32 parameters in place and they are
+    all-gathered in fp32.  bfloat16 halves the all-gather: the model's
+    parameters become bf16 views of the flat buffer, each rank keeps its
+    shard's fp32 master parameters, and the step kernel itself writes the
+    updated shard rounded to bf16 into the flat buffer, which is the
+    all-gather's send buffer (gradients are then bf16 too).
+
+    The all-gather runs per bucket, each started as soon as the bucket's
+    step kernel is queued, so it overlaps the step of the buckets after it.
+    With ``overlap_param_gather`` step() returns without waiting for them:
+    call ``attach(model)`` once, and each module's forward waits (a forward
+    pre-hook) for the buckets holding its own parameters, so the gathers
+    overlap the next forward; ``wait_param_gather()`` waits for all.
+    ``profile_phases`` records CUDA events around the reduce-scatter, the
+    step kernels and the all-gather; ``last_phase_ms()`` reads them.
     """
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  alpha=0.9, layer_count=24, batch_size=32, update_freq=20, block_size=256,
                  *, process_group=None, grad_dtype=torch.float32, bucket_elems=None,
-                 overlap_grad_reduce=False, **kw):
+                 overlap_grad_reduce=False, param_dtype=torch.float32,
+                 overlap_param_gather=False, profile_phases=False, **kw):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                          alpha=alpha, layer_count=layer_count, batch_size=batch_size,
                          update_freq=update_freq, block_size=block_size, **kw)
@@ -160,10 +179,30 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         for p in self.params:
             if p.dtype != torch.float32:
                 raise RuntimeError("MDQ parameters must be float32")
+        if param_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("param_dtype must be torch.float32 or torch.bfloat16")
+        if param_dtype == torch.bfloat16:
+            grad_dtype = torch.bfloat16
+        self.param_dtype = param_dtype
         dev = self.params[0].device
         self.layout = ShardLayout([p.numel() for p in self.params], self.block, self.world,
                                   bucket_elems)
-        self.flat_param = torch.zeros(self.layout.total, dtype=torch.float32, device=dev)
+        self.pieces = self.layout.pieces(self.rank)
+        # fp32 master parameters of this rank's shards (bf16 parameters only):
+        # bucket k's shard at [master_base[k], master_base[k] + shard_k).
+        self.master = None
+        self.master_base = []
+        if param_dtype == torch.bfloat16:
+            base = 0
+            for b in self.layout.buckets:
+                self.master_base.append(base)
+                base += b.shard
+            self.master = torch.zeros(base, dtype=torch.float32, device=dev)
+            for pc in self.pieces:
+                mo = self._master_off(pc)
+                src = self.params[pc.param].detach().reshape(-1)[pc.start:pc.start + pc.n]
+                self.master[mo:mo + pc.n].copy_(src)
+        self.flat_param = torch.zeros(self.layout.total, dtype=param_dtype, device=dev)
         self.flat_grad = torch.zeros(self.layout.total, dtype=grad_dtype, device=dev)
         for p, off in zip(self.params, self.layout.offsets):
             n = p.numel()
@@ -172,7 +211,11 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             if grad_dtype != p.dtype and hasattr(p, "grad_dtype"):
                 p.grad_dtype = grad_dtype  # low-precision gradients of fp32 parameters
             p.grad = self.flat_grad[off:off + n].view_as(p)
-        self.pieces = self.layout.pieces(self.rank)
+        self.overlap_param_gather = bool(overlap_param_gather)
+        self._ag_works = [None] * len(self.layout.buckets)
+        self._module_hooks = []
+        self.profile_phases = bool(profile_phases)
+        self._phase_events = None
         self._descs = None
         # Asynchronous bucket reduce-scatters launched during backward.
         self._bucket_of = [0] * len(self.params)
@@ -236,9 +279,30 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             st["piece"] = (pc.start, pc.n)
         return st
 
+    def _master_off(self, pc: Piece) -> int:
+        k = self._bucket_of_piece(pc)
+        lo, _ = self.layout.shard_range(self.layout.buckets[k], self.rank)
+        return self.master_base[k] + (pc.flat_off - lo)
+
+    def _bucket_of_piece(self, pc: Piece) -> int:
+        for k, b in enumerate(self.layout.buckets):
+            if b.first <= pc.param < b.last:
+                return k
+        raise KeyError(pc.param)
+
     def _piece_views(self, pc: Piece):
+        """(fp32 parameters the step updates, gradient) of one local piece."""
         a, e = pc.flat_off, pc.flat_off + pc.n
+        if self.master is not None:
+            mo = self._master_off(pc)
+            return self.master[mo:mo + pc.n], self.flat_grad[a:e]
         return self.flat_param[a:e], self.flat_grad[a:e]
+
+    def master_params(self):
+        """This rank's fp32 parameters of each local piece, as
+        {param index: (start within the parameter, fp32 tensor)}: the
+        master copy with bf16 parameters, else views of the parameters."""
+        return {pc.param: (pc.start, self._piece_views(pc)[0]) for pc in self.pieces}
 
     # ------------------------------------------------------------------
     def _reduce_scatter_bucket(self, b: Bucket, async_op: bool = False):
@@ -269,18 +333,60 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             self._works[k] = None
             self._ready[k] = 0
 
-    def _all_gather_params(self):
+    def _all_gather_bucket(self, k: int):
+        """Start the all-gather of bucket k's updated parameters (in place in
+        the flat parameter buffer); the work is kept in _ag_works[k]."""
         if self.world == 1:
             return
-        nccl = dist.get_backend(self.group) == "nccl"
-        for b in self.layout.buckets:
-            full = self.flat_param[b.base:b.base + b.shard * self.world]
-            lo, hi = self.layout.shard_range(b, self.rank)
-            if nccl:
-                dist.all_gather_into_tensor(full, self.flat_param[lo:hi], group=self.group)
-            else:
-                parts = list(full.chunk(self.world))
-                dist.all_gather(parts, self.flat_param[lo:hi].clone(), group=self.group)
+        b = self.layout.buckets[k]
+        full = self.flat_param[b.base:b.base + b.shard * self.world]
+        lo, hi = self.layout.shard_range(b, self.rank)
+        if dist.get_backend(self.group) == "nccl":
+            w = dist.all_gather_into_tensor(full, self.flat_param[lo:hi], group=self.group,
+                                            async_op=True)
+        else:
+            parts = list(full.chunk(self.world))
+            w = dist.all_gather(parts, self.flat_param[lo:hi].clone(), group=self.group,
+                                async_op=True)
+        self._ag_works[k] = w
+
+    def _wait_bucket(self, k: int):
+        w = self._ag_works[k]
+        if w is not None:
+            self._ag_works[k] = None
+            w.wait()
+
+    def wait_param_gather(self):
+        """Wait for every pending parameter all-gather (on the current stream)."""
+        for k in range(len(self._ag_works)):
+            self._wait_bucket(k)
+
+    def attach(self, model: torch.nn.Module):
+        """Make each module's forward wait for the all-gathers of the buckets
+        that hold its own parameters (for ``overlap_param_gather``)."""
+        index = {id(p): i for i, p in enumerate(self.params)}
+        for mod in model.modules():
+            ks = sorted({self._bucket_of[index[id(p)]] for p in mod.parameters(recurse=False)
+                         if id(p) in index})
+            if ks:
+                def pre_hook(_m, _args, ks=ks):
+                    for k in ks:
+                        self._wait_bucket(k)
+                self._module_hooks.append(mod.register_forward_pre_hook(pre_hook))
+
+    def last_phase_ms(self):
+        """Device time of the latest step's phases (``profile_phases``):
+        reduce_scatter (waiting for the gradient reduce-scatters), step (the
+        fused step kernels, queued bucket after bucket with the all-gathers
+        of earlier buckets running beside them), all_gather_tail (what of
+        the all-gathers remained after the last step kernel) and total."""
+        ev = self._phase_events
+        if ev is None:
+            return None
+        ev[-1].synchronize()
+        a, b, c, d = ev
+        return {"reduce_scatter": a.elapsed_time(b), "step": b.elapsed_time(c),
+                "all_gather_tail": c.elapsed_time(d), "total": a.elapsed_time(d)}
 
     def _global_grad_stats(self):
         """Per-parameter [n_l, r_l, v_l] from all-reduced partial sums."""
@@ -344,7 +450,16 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         self.last_step_timings = {"quant_dequant_unpack_ms": 0.0, "quant_dequant_pack_ms": 0.0,
                                   "mdq_fused_io_fast_path_params": 0,
                                   "mdq_fused_io_fallback_params": 0}
+        ev = None
+        if self.profile_phases and self.flat_param.is_cuda:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
+        # A pending all-gather of the previous step must land before the
+        # parameters are touched again.
+        self.wait_param_gather()
         self._reduce_scatter_grads()
+        if ev is not None:
+            ev[1].record()
         for pc in self.pieces:
             self._piece_state(pc)
         # A rank without a piece of some parameter still needs its step counter
@@ -359,35 +474,51 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         if self.fixed_bits is None and ((self.total_steps % uf == 0) or self.total_steps < 5):
             self._decide_bits_sharded()
 
-        items, repack = [], []
         held = {pc.param: pc for pc in self.pieces}
-        for i, p in enumerate(self.params):
-            st = self.state[p]
-            if i not in held:
-                # Same step counting as the holders (FusedIO, incl. the double
-                # increment when the storage would have to change layout).
-                bits = int(st["current_bit"])
-                st["step"] += 1
-                st.setdefault("_layout_bits", 16 if self.fixed_bits is None else bits)
-                if self.fixed_bits is None and st["_layout_bits"] != bits:
-                    st["step"] += 1
-                    st["_layout_bits"] = bits
-                continue
-            pc = held[i]
-            pv, gv = self._piece_views(pc)
-            first = len(items)
-            # The shared FusedIO logic (step counting, storage align / pack)
-            # runs on the piece's state; its step item then points at the
-            # piece's views of the flat buffers.
-            self._prepare_param(p, self.param_group_of[i], items, repack)
-            for it in items[first:]:
-                it.p, it.grad = pv, gv
-            st["_layout_bits"] = int(st["current_bit"])
         device = self.flat_param.device
-        self._launch(items, device)
-        for st, bits in repack:
-            self._pack_momentum_storage(st, bits)
-        self._all_gather_params()
+        # Bucket by bucket: queue the fused step of the bucket's local pieces,
+        # then start its all-gather, which runs while later buckets step.
+        for k, b in enumerate(self.layout.buckets):
+            items, repack = [], []
+            for i in range(b.first, b.last):
+                p = self.params[i]
+                st = self.state[p]
+                if i not in held:
+                    # Same step counting as the holders (FusedIO, incl. the
+                    # double increment when the storage would change layout).
+                    bits = int(st["current_bit"])
+                    st["step"] += 1
+                    st.setdefault("_layout_bits", 16 if self.fixed_bits is None else bits)
+                    if self.fixed_bits is None and st["_layout_bits"] != bits:
+                        st["step"] += 1
+                        st["_layout_bits"] = bits
+                    continue
+                pc = held[i]
+                pv, gv = self._piece_views(pc)
+                first = len(items)
+                # The shared FusedIO logic (step counting, storage align /
+                # pack) runs on the piece's state; its step item then points
+                # at the piece's views of the flat buffers.
+                self._prepare_param(p, self.param_group_of[i], items, repack)
+                for it in items[first:]:
+                    it.p, it.grad = pv, gv
+                    if self.master is not None:
+                        a = pc.flat_off
+                        it.p_bf16 = self.flat_param[a:a + pc.n]
+                st["_layout_bits"] = int(st["current_bit"])
+            self._launch(items, device)
+            for st, bits in repack:
+                self._pack_momentum_storage(st, bits)
+            self._all_gather_bucket(k)
+        if ev is not None:
+            ev[2].record()
+        if not self.overlap_param_gather:
+            self.wait_param_gather()
+        if ev is not None:
+            if self.overlap_param_gather:
+                self.wait_param_gather()  # (profiling: the phases need an end)
+            ev[3].record()
+            self._phase_events = ev
         return loss
 
     def load_consolidated_state_dict(self, state_dict):

@@ -129,20 +129,21 @@ def test_descriptor_packing_matches_the_ctypes_mirror():
     from mdq_b200 import kernels
     from mdq_b200._lib import TensorDesc
 
-    assert kernels._DESC_FMT.size <= ctypes.sizeof(TensorDesc)
+    assert kernels._DESC_FMT.size == ctypes.sizeof(TensorDesc) == 120
     expect_off = {"p": 0, "grad": 8, "exp_avg": 16, "exp_avg_sq": 24, "scale_m": 32, "scale_v": 40,
                   "v_min": 48, "n": 56, "step": 64, "block": 68, "lr": 72, "weight_decay": 76,
                   "eps": 80, "beta1": 84, "beta2": 88, "m_bits": 92, "v_bits": 96, "layout": 100,
-                  "grad_dtype": 104}
+                  "grad_dtype": 104, "p_bf16": 112}
     for name, off in expect_off.items():
         assert getattr(TensorDesc, name).offset == off, name
     p = torch.zeros(1000)
     t = [torch.zeros(1000, dtype=torch.uint8), torch.zeros(4), torch.zeros(4), torch.zeros(4)]
-    for easq in (None, torch.zeros(1000, dtype=torch.uint8)):
+    p16 = torch.zeros(1000, dtype=torch.bfloat16)
+    for easq, copy in ((None, None), (torch.zeros(1000, dtype=torch.uint8), p16)):
         it = kernels.StepItem(p=p, grad=torch.zeros(1000, dtype=torch.bfloat16), exp_avg=t[0],
                               exp_avg_sq=easq, scale_m=t[1], scale_v=t[2], v_min=t[3], step=7,
                               block=256, lr=3e-4, weight_decay=0.1, eps=1e-8, beta1=0.9,
-                              beta2=0.95, m_bits=8, v_bits=4, layout=4)
+                              beta2=0.95, m_bits=8, v_bits=4, layout=4, p_bf16=copy)
         d = TensorDesc()
         kernels.fill_desc(d, it)
         assert (d.p, d.grad, d.exp_avg, d.scale_m, d.scale_v, d.v_min) == (
@@ -151,6 +152,7 @@ def test_descriptor_packing_matches_the_ctypes_mirror():
         assert (d.exp_avg_sq or 0) == (easq.data_ptr() if easq is not None else 0)
         assert (d.n, d.step, d.block, d.m_bits, d.v_bits, d.layout) == (1000, 7, 256, 8, 4, 4)
         assert d.grad_dtype == kernels._DTYPE_CODE[torch.bfloat16]
+        assert (d.p_bf16 or 0) == (copy.data_ptr() if copy is not None else 0)
         for name, val in (("lr", 3e-4), ("weight_decay", 0.1), ("eps", 1e-8), ("beta1", 0.9),
                           ("beta2", 0.95)):
             assert getattr(d, name) == ctypes.c_float(val).value, name

@@ -252,3 +252,22 @@ def test_long_trajectory_bit_exact(ref, cuda_device, layout, bits, block):
     torch.cuda.synchronize()
     mm = a.mismatches(b)
     assert all(v == 0 for v in mm.values()), mm
+
+
+@pytest.mark.parametrize("layout,bits,n,block", [("packed4", 4, (1 << 20) + 77, 256),
+                                                  ("s8u8", 8, 100_003, 1024),
+                                                  ("s16u16", 16, 5_000, 100)])
+def test_bf16_parameter_copy(cuda_device, layout, bits, n, block):
+    """p_bf16 receives the updated parameters rounded to bf16; everything else
+    is what the same step without the copy produces."""
+    a = State(n, block, layout, cuda_device, seed=11)
+    b = a.clone()
+    p16 = torch.full((n,), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    for s, g in enumerate(grads(n, 3, cuda_device, torch.bfloat16, seed=12), start=1):
+        kernels.step_multi([item_of(a, g, s, bits, bits, LAYOUT_ID[layout])], p_mode=P_FAST)
+        it = item_of(b, g, s, bits, bits, LAYOUT_ID[layout])
+        it.p_bf16 = p16
+        kernels.step_multi([it], p_mode=P_FAST)
+        torch.cuda.synchronize()
+        assert all(v == 0 for v in a.mismatches(b).values())
+        assert torch.equal(p16.view(torch.int16), b.p.to(torch.bfloat16).view(torch.int16))

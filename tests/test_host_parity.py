@@ -31,6 +31,8 @@ def oracle_launch(self, items, device):
                     it.exp_avg.numpy(), v, it.scale_m.numpy(), it.scale_v.numpy(),
                     it.v_min.numpy(), it.block, it.beta1, it.beta2, it.lr, it.weight_decay,
                     it.eps, it.step, it.m_bits, it.v_bits)
+        if getattr(it, "p_bf16", None) is not None:
+            it.p_bf16.copy_(it.p.to(torch.bfloat16))
 
 
 def cpu_fused_stats(self, params_with_grad):

@@ -299,3 +299,111 @@ def test_bucketed_overlap_equals_unsharded(world, kw):
         for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
             np.testing.assert_array_equal(rs[k].numpy().view(np.uint8), st[k].view(np.uint8),
                                           err_msg=f"param {i} {k}")
+
+
+class _Term(torch.nn.Module):
+    """One parameter and its loss term <p, c> (a module, so ZeroMDQAdamW.attach
+    can put a forward pre-hook on it)."""
+
+    def __init__(self, p):
+        super().__init__()
+        self.p = p
+
+    def forward(self, c):
+        return (self.p * c).sum()
+
+
+def _bf16_grads(rank, step, sizes):
+    # Small multiples of 2^-12: every value, sum over two ranks and average is
+    # exact in bfloat16, so gloo's bf16 reduction matches the reference's.
+    g = torch.Generator().manual_seed(1000 * step + rank)
+    return [torch.round(torch.randn(n, generator=g) * 8).clamp(-31, 31) / 2 ** 12 for n in sizes]
+
+
+def _bf16_worker(rank, world, port, steps, kw, sizes, q):
+    """bf16 parameters, fp32 master shards, bucketed all-gathers left running
+    after step() and waited for by the next forward's pre-hooks."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _use_oracle()
+        from mdq_b200.zero1 import ZeroMDQAdamW
+
+        torch.set_num_threads(1)
+        params = _params(sizes)
+        model = torch.nn.ModuleList([_Term(p) for p in params])
+        opt = ZeroMDQAdamW([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
+                           lr=1e-3, weight_decay=0.01, block_size=256, bucket_elems=3000,
+                           param_dtype=torch.bfloat16, overlap_param_gather=True, **kw)
+        opt.attach(model)
+        assert all(p.dtype == torch.bfloat16 for p in params)
+        assert len(opt.layout.buckets) > 2
+        for t in range(1, steps + 1):
+            opt.zero_grad()
+            coef = [c.to(torch.bfloat16) for c in _bf16_grads(rank, t, sizes)]
+            sum(m(c) for m, c in zip(model, coef)).backward()
+            opt.step()
+            if t < steps:
+                assert any(w is not None for w in opt._ag_works)  # still in flight
+        model[0](torch.zeros_like(params[0]))  # a forward waits for its bucket
+        opt.wait_param_gather()
+        masters = [None] * world
+        local = {i: (s, m.numpy().copy()) for i, (s, m) in opt.master_params().items()}
+        dist.all_gather_object(masters, local)
+        sd = opt.consolidated_state_dict()
+        if rank == 0:
+            full = [np.zeros(n, np.float32) for n in sizes]
+            for part in masters:
+                for i, (s, m) in part.items():
+                    full[i][s:s + m.size] = m
+            q.put(([p.detach().float().numpy().copy() for p in params], full,
+                   {i: {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in st.items()}
+                    for i, st in sd["state"].items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bf16_params_fp32_master_overlapped_gather():
+    """bf16 model parameters: every rank's parameters are the bf16 rounding of
+    the fp32 master weights, and those equal the unsharded fp32 run's
+    parameters bit for bit (as do codes and scales)."""
+    world, steps, kw = 2, 4, dict(fixed_bits=(8, 4))
+    sizes = SIZES
+    _use_oracle()
+    from mdq_b200.optim import MDQAdamWSimpleFusedIO
+
+    torch.set_num_threads(1)
+    ref_params = _params(sizes)
+    ref_opt = MDQAdamWSimpleFusedIO([{"params": ref_params[:4]},
+                                     {"params": ref_params[4:], "weight_decay": 0.0}],
+                                    lr=1e-3, weight_decay=0.01, block_size=256, **kw)
+    for t in range(1, steps + 1):
+        per_rank = [_bf16_grads(r, t, sizes) for r in range(world)]
+        for i, p in enumerate(ref_params):
+            p.grad_dtype = torch.bfloat16
+            p.grad = (sum(pr[i] for pr in per_rank) / world).to(torch.bfloat16)
+        ref_opt.step()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bf16_worker, args=(r, world, port, steps, kw, sizes, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    model_params, masters, state = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for i, p in enumerate(ref_params):
+        want = p.detach().numpy()
+        np.testing.assert_array_equal(masters[i].view(np.int32), want.view(np.int32),
+                                      err_msg=f"master {i}")
+        np.testing.assert_array_equal(model_params[i],
+                                      p.detach().to(torch.bfloat16).float().numpy(),
+                                      err_msg=f"bf16 param {i}")
+        rs, st = ref_opt.state[p], state[i]
+        assert st["step"] == rs["step"], i
+        for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
+            np.testing.assert_array_equal(rs[k].numpy().view(np.uint8), st[k].view(np.uint8),
+                                          err_msg=f"param {i} {k}")
