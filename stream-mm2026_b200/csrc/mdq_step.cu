@@ -447,7 +447,7 @@ mdq_status mdq_fused_adamw(float* p, const void* grad, int32_t grad_dtype, void*
                            cudaStream_t stream) {
     g_err[0] = '\0';
     if (block_size < 1) return fail(MDQ_ERR_INVALID_ARG, "block_size must be >= 1");
-    mdq_tensor_desc d;
+    mdq_tensor_desc d = {};  // every field not set below (p_bf16) stays zero
     d.p = p;
     d.grad = grad;
     d.exp_avg = exp_avg;
