@@ -73,26 +73,69 @@ def measured_peak():
 # clocks sampled during the timed region
 # ----------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and throttle reasons of one GPU, sampled every 10 ms through
+    NVML while the timed region runs (reading only; nothing is set).  Falls
+    back to nvidia-smi every 200 ms when NVML is unavailable."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
+        self.sm, self.max_mhz, self.reasons = [], None, set()
         self._stop = threading.Event()
+        self._nvml = self._handle()
         self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _handle(self):
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            try:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except pynvml.NVMLError:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            return h
+        except Exception:  # noqa: BLE001 (no NVML: use nvidia-smi)
+            return None
+
+    def _sample_nvml(self):
+        import pynvml
+
+        self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(self._nvml, pynvml.NVML_CLOCK_SM)))
+        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self._nvml)
+        for name, const in self.REASONS:
+            if bits & getattr(pynvml, const, 0):
+                self.reasons.add(name)
+
+    def _sample_smi(self):
+        out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                              "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=5).stdout.strip()
+        s = [x.strip() for x in out.split(",")]
+        self.sm.append(float(s[0]))
+        self.max_mhz = float(s[1])
+        for (name, _), val in zip(self.REASONS, s[3:7]):
+            if val.lower() == "active":
+                self.reasons.add(name)
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}",
-                                      f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
-                                     capture_output=True, text=True, timeout=5).stdout.strip()
-                self.samples.append([x.strip() for x in out.split(",")])
-            except (OSError, subprocess.SubprocessError):
+                self._sample_nvml() if self._nvml is not None else self._sample_smi()
+            except Exception:  # noqa: BLE001 (a failed read is skipped)
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.01 if self._nvml is not None else 0.2)
 
     def __enter__(self):
         self._t.start()
@@ -103,19 +146,9 @@ class ClockSampler:
         self._t.join(timeout=10)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for s in self.samples:
-            try:
-                sm.append(float(s[0]))
-                mx = float(s[1])
-                for name, val in zip(names, s[3:7]):
-                    if val.strip().lower() == "active":
-                        reasons.add(name)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.sm), "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------
@@ -423,16 +456,18 @@ def nccl_busbw(world, device, nbytes=1 << 30):
 
     if world == 1:
         return None
-    n = nbytes // 2
-    full = torch.empty(n, dtype=torch.bfloat16, device=device)
-    shard = full[: n // world]
+    n = nbytes // 2 // world * world
+    full = torch.zeros(n, dtype=torch.bfloat16, device=device)
+    rank = dist.get_rank()
+    own = full[rank * (n // world):(rank + 1) * (n // world)]   # in place, as ZeRO uses it
+    out = torch.empty(n // world, dtype=torch.bfloat16, device=device)
     res = {}
     for name in ("all_gather", "reduce_scatter"):
         def op():
             if name == "all_gather":
-                dist.all_gather_into_tensor(full, shard)
+                dist.all_gather_into_tensor(full, own)
             else:
-                dist.reduce_scatter_tensor(shard, full, op=dist.ReduceOp.AVG)
+                dist.reduce_scatter_tensor(out, full, op=dist.ReduceOp.AVG)
         for _ in range(3):
             op()
         torch.cuda.synchronize()
@@ -444,8 +479,8 @@ def nccl_busbw(world, device, nbytes=1 << 30):
         torch.cuda.synchronize()
         ms = _max_over_ranks([a.elapsed_time(b) / 10], device, world)[0]
         res[name + "_busbw_gbs"] = round((world - 1) / world * nbytes / (ms * 1e-3) / 1e9, 1)
-    res["bytes"] = nbytes
-    del full
+    res["bytes"] = n * 2
+    del full, out
     torch.cuda.empty_cache()
     return res
 

@@ -1,0 +1,355 @@
+// mdq_blocks.cuh - the warp-per-block fused-step kernel for quantisation
+// blocks of 512 or 1024 elements.
+//
+// In the tiled kernel (mdq_tiles.cuh) a block wider than one warp's span of
+// 32 x PT elements is shared by several warps, which exchange their partial
+// extremes through shared memory behind a named barrier on every tile, and
+// every thread evaluates the block's requantisation constants (two logf, an
+// IEEE divide, two reciprocals) for only PT elements.  Here one warp owns a
+// whole block: it walks the block in S = B / 256 sub-tiles of 8 elements per
+// lane (the stripe layout: lane r holds elements 128 i + 4 r + 0..3 of a
+// sub-tile, i = 0, 1, so every warp access covers whole 32-byte sectors),
+//   pass 1: loads p, g and the codes of a sub-tile, dequantises with the
+//           block's old scales, applies AdamW, stores p, and parks the new m
+//           and x = v + 1e-12 in the warp's slice of shared memory (each lane
+//           reads back only what it wrote, so no barrier is needed);
+//   then:   reduces max|m|, max x, min x over the warp with redux.sync and
+//           computes the block's constants once per 32 S elements per lane;
+//   pass 2: requantises the parked m and x and stores the codes.
+// Warps work independently (no CTA barrier at all); a CTA of 8 warps takes 8
+// consecutive blocks at a time, so it streams 8 B contiguous elements.
+#pragma once
+
+#include "mdq_tiles.cuh"
+
+namespace mdq {
+
+constexpr int kBlkWarps = 8;
+constexpr int kBlkThreads = 32 * kBlkWarps;
+
+// Shared-memory bytes of one CTA for blocks of 2^LOGB elements.
+template <int LOGB> constexpr int blocks_smem_bytes() {
+    return kBlkWarps * (2 << LOGB) * (int)sizeof(float);
+}
+
+// One quantisation block (unit) of the tensor in X, starting at element e0.
+// FULL: all B elements in range and all pointers allow vector access.
+template <int LAYOUT, typename GT, bool EXACT_P, bool FULL, int LOGB, bool TBL>
+__device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* wm, float* wx) {
+    using CI = Codes<LAYOUT>;
+    using TC = TableCodes<LAYOUT>;
+    constexpr int B = 1 << LOGB;
+    constexpr int S = B / 256;
+    constexpr bool kApprox = CI::kApproxLog;
+    constexpr bool kMagicC = CI::kMagicCodes;
+    constexpr bool kTab = TBL && FULL;
+    constexpr int kB = CI::kMBias;
+    const float kNaN = __int_as_float(0x7fffffff);
+    const int lane = threadIdx.x & 31;
+    const TensorPtrs T = X.t;
+    const StepConsts& C = X.C;
+    const int64_t n = X.n;
+    const int64_t blk = e0 >> LOGB;
+
+    const float sm = T.sm[blk], sv = T.sv[blk], vmn = T.vmin[blk];
+    float tv = 0.0f, tm = 0.0f;
+    if constexpr (kTab) {
+        const float kf = small_int_to_float(lane & 15);
+        tv = dequant_v(kf, sv, vmn);
+        tm = __fmul_rn(__fsub_rn(kf, 8.0f), sm);
+    }
+    float s0 = kNaN, s1 = kNaN, s2 = kNaN;
+
+    // ---- pass 1: dequantise, AdamW, parameter update ---------------------
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        int cnt[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            cnt[i] = 4;
+            if (!FULL) {
+                const int64_t rem = n - (e0 + 256 * s + 128 * i + 4 * lane);
+                cnt[i] = rem >= 4 ? 4 : (rem > 0 ? (int)rem : 0);
+            }
+        }
+        float p[8], g[8], m[8], v[8];
+        int qm[8], qv[8];
+        typename TC::Raw raw[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
+            if (FULL) {
+                const float4 a = __ldcs(reinterpret_cast<const float4*>(T.p + e));
+                p[4 * i + 0] = a.x; p[4 * i + 1] = a.y; p[4 * i + 2] = a.z; p[4 * i + 3] = a.w;
+                float gg[4];
+                Grad<GT>::load4(T.g, e, gg);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) g[4 * i + j] = gg[j];
+                if constexpr (kTab) {
+                    TC::load4(T, e, raw[i]);
+                } else {
+                    int am[4], av[4];
+                    CI::load4(T, e, am, av);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) { qm[4 * i + j] = am[j]; qv[4 * i + j] = av[j]; }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int k = 4 * i + j;
+                    p[k] = 0.0f; g[k] = 0.0f; qm[k] = 0; qv[k] = 0;
+                    if (j < cnt[i]) {
+                        p[k] = T.p[e + j];
+                        g[k] = Grad<GT>::load1(T.g, e + j);
+                        CI::load1(T, e + j, qm[k], qv[k]);
+                    }
+                }
+            }
+        }
+        if constexpr (kTab) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    m[4 * i + j] = TC::m(raw[i], j, tm, sm);
+                    v[4 * i + j] = TC::v(raw[i], j, tv);
+                }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float qmf = kMagicC ? small_int_to_float(qm[k]) : (float)qm[k];
+                m[k] = __fmul_rn(qmf, sm);
+                const float qvf = kMagicC ? small_int_to_float(qv[k]) : (float)(unsigned)qv[k];
+                v[k] = dequant_v(qvf, sv, vmn);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            m[k] = adam_m(m[k], g[k], C);
+            v[k] = adam_v(v[k], g[k], C);
+            p[k] = update_p<EXACT_P>(p[k], m[k], v[k], C);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
+            if (FULL) {
+                __stcs(reinterpret_cast<float4*>(T.p + e),
+                       make_float4(p[4 * i + 0], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]));
+                if (T.p16 != nullptr) {
+                    const __nv_bfloat162 lo = __floats2bfloat162_rn(p[4 * i + 0], p[4 * i + 1]);
+                    const __nv_bfloat162 hi = __floats2bfloat162_rn(p[4 * i + 2], p[4 * i + 3]);
+                    uint2 w;
+                    w.x = *reinterpret_cast<const unsigned*>(&lo);
+                    w.y = *reinterpret_cast<const unsigned*>(&hi);
+                    __stcs(reinterpret_cast<uint2*>(T.p16 + e), w);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < cnt[i]) {
+                        T.p[e + j] = p[4 * i + j];
+                        if (T.p16 != nullptr) T.p16[e + j] = __float2bfloat16_rn(p[4 * i + j]);
+                    }
+            }
+        }
+        // Block statistics (CUDA/stquant_kernel.cu:184-199): |m|, and x =
+        // v + 1e-12 whose logf extremes are logf of its extremes; elements
+        // past the end enter as |m| = 0 and x = 1 (log v = 0, :92-93).
+        float x[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const bool ok = FULL || (k & 3) < cnt[k / 4];
+            x[k] = ok ? __fadd_rn(v[k], 1e-12f) : 1.0f;
+            if (!ok) m[k] = 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k += 2) {
+            s0 = max3f(s0, fabsf(m[k]), fabsf(m[k + 1]));
+            s1 = max3f(s1, x[k], x[k + 1]);
+            s2 = min3f(s2, x[k], x[k + 1]);
+        }
+        // Park m and x for pass 2 (this lane's own slots).
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int o = 256 * s + 128 * i + 4 * lane;
+            *reinterpret_cast<float4*>(wm + o) =
+                make_float4(m[4 * i + 0], m[4 * i + 1], m[4 * i + 2], m[4 * i + 3]);
+            *reinterpret_cast<float4*>(wx + o) =
+                make_float4(x[4 * i + 0], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+        }
+    }
+
+    asm volatile("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(s0));
+    asm volatile("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(s1));
+    asm volatile("redux.sync.min.f32 %0, %0, 0xffffffff;" : "+f"(s2));
+    const QConsts Q = make_q<kApprox, kB>(s0, s1, s2, C);
+    if (lane == 0) {
+        T.sm[blk] = Q.new_sm;
+        T.sv[blk] = Q.new_sv;
+        T.vmin[blk] = Q.lmin;
+    }
+
+    // ---- pass 2: requantise (CUDA/stquant_kernel.cu:204-216) ---------------
+    constexpr bool kCorrect = !kApprox;
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        float m[8], x[8];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int o = 256 * s + 128 * i + 4 * lane;
+            const float4 a = *reinterpret_cast<const float4*>(wm + o);
+            const float4 b = *reinterpret_cast<const float4*>(wx + o);
+            m[4 * i + 0] = a.x; m[4 * i + 1] = a.y; m[4 * i + 2] = a.z; m[4 * i + 3] = a.w;
+            x[4 * i + 0] = b.x; x[4 * i + 1] = b.y; x[4 * i + 2] = b.z; x[4 * i + 3] = b.w;
+        }
+        int mw[8], vw[8];
+        float rem_m = 0.0f, rem_v = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float rr;
+            mw[k] = min(round_checked<kCorrect, kB>(__fmul_rn(m[k], Q.rdm), m[k], Q.dm,
+                                                    Q.half_dm, rr), Q.mw_hi);
+            rem_m = max_nan(rem_m, rr);
+            const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -Q.lmin)
+                                     : __fsub_rn(logf(x[k]), Q.lmin);
+            vw[k] = round_checked<kCorrect>(__fmul_rn(xv, Q.rdv), xv, Q.dv, Q.half_dv, rr);
+            rem_v = max_nan(rem_v, rr);
+        }
+        if (!kMagicC || !(rem_m < Q.half_dm && rem_v < Q.thr_v)) {
+            // Rare: codes that fail their check take the reference's
+            // double-precision expression (all of them for 32-bit codes).
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                float rr;
+                round_checked<kCorrect>(__fmul_rn(m[k], Q.rdm), m[k], Q.dm, Q.half_dm, rr);
+                if (!kMagicC || !(rr < Q.half_dm)) mw[k] = CI::m_word(requant_m_ref(m[k], Q.dm, C.lm_d));
+                const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -Q.lmin)
+                                         : __fsub_rn(logf(x[k]), Q.lmin);
+                round_checked<kCorrect>(__fmul_rn(xv, Q.rdv), xv, Q.dv, Q.half_dv, rr);
+                if (!kMagicC || !(rr < Q.thr_v))
+                    vw[k] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[k]), Q.lmin), Q.dv, C.lv_d));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
+            int a4[4], b4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { a4[j] = mw[4 * i + j]; b4[j] = vw[4 * i + j]; }
+            if (FULL) {
+                CI::store4(T, e, a4, b4);
+            } else {
+                const int64_t rem = n - e;
+                const int c = rem >= 4 ? 4 : (rem > 0 ? (int)rem : 0);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < c) CI::store1(T, e + j, a4[j], b4[j]);
+            }
+        }
+    }
+}
+
+// Persistent grid: CTA c takes units [total c / grid, total (c+1) / grid),
+// warp w the units lo + w, lo + w + 8, ...; `tile_begin` of a descriptor
+// counts units (blocks) here.  Each warp stages the tensor it works on in its
+// own shared-memory slot.
+template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL>
+__global__ void __launch_bounds__(kBlkThreads, 3)
+mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
+    extern __shared__ __align__(16) float s_park[];
+    __shared__ TileCtx s_wctx[kBlkWarps];
+    const int w = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    float* wm = s_park + (size_t)w * (2 << LOGB);
+    float* wx = wm + (1 << LOGB);
+    TileCtx& X = s_wctx[w];
+    const int64_t total = P.total_tiles;
+    const int lo = (int)(total * blockIdx.x / gridDim.x);
+    const int hi = (int)(total * (blockIdx.x + 1) / gridDim.x);
+    int cur_end = -1;
+    for (int u = lo + w; u < hi; u += kBlkWarps) {
+        if (u >= cur_end) {
+            __syncwarp();
+            if (lane == 0) {
+                const LaunchDesc& D = P.d[find_desc(P, u)];
+                X.t = D.t;
+                X.n = D.n;
+                X.tile_begin = D.tile_begin;
+                X.tile_end = D.tile_begin + (int32_t)((D.n + (1 << LOGB) - 1) >> LOGB);
+                X.lb = LOGB;
+                X.vec = D.vec;
+                X.C = make_step_consts(D.b1, D.b2, D.lr, D.wd, D.eps, D.step, D.m_bits,
+                                       D.v_bits);
+            }
+            __syncwarp();
+            cur_end = X.tile_end;
+        }
+        const int64_t e0 = (int64_t)(u - X.tile_begin) << LOGB;
+        if (X.vec && e0 + (1 << LOGB) <= X.n)
+            block_body<LAYOUT, GT, EXACT_P, true, LOGB, TBL>(X, e0, wm, wx);
+        else
+            block_body<LAYOUT, GT, EXACT_P, false, LOGB, TBL>(X, e0, wm, wx);
+    }
+}
+
+template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL>
+mdq_status launch_blocks_t(const LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
+    auto k = mdq_step_blocks<LAYOUT, GT, EXACT_P, CAP, LOGB, TBL>;
+    constexpr int kSmem = blocks_smem_bytes<LOGB>();
+    static int occ = 0;  // per instantiation; identical across B200 devices
+    if (occ == 0) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess)
+            return mdq_fail(MDQ_ERR_CUDA, "block kernel smem attribute: %s", cudaGetErrorString(e));
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, kBlkThreads, kSmem) != cudaSuccess ||
+            b < 1)
+            b = 1;
+        occ = b;
+    }
+    int64_t grid = (int64_t)sms * occ;
+    const int64_t ctas_needed = (P.total_tiles + kBlkWarps - 1) / kBlkWarps;
+    if (grid > ctas_needed) grid = ctas_needed;
+    if (grid < 1) grid = 1;
+    k<<<(unsigned)grid, kBlkThreads, kSmem, stream>>>(P);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return mdq_fail(MDQ_ERR_CUDA, "block step launch: %s", cudaGetErrorString(e));
+    return MDQ_OK;
+}
+
+// Blocks of 2^LOGB (9 or 10) elements; tables for 4-bit v codes.
+template <int LAYOUT, typename GT, int CAP>
+mdq_status launch_blocks_mode(const LaunchParams<CAP>& P, bool exact, int logb, int sms,
+                              cudaStream_t s) {
+    constexpr bool kV4 = LAYOUT == MDQ_LAYOUT_PACKED4 || LAYOUT == MDQ_LAYOUT_M8V4;
+    constexpr bool kT = kV4 && MDQ_USE_TABLES != 0;
+    if (logb == 10)
+        return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 10, kT>(P, sms, s)
+                     : launch_blocks_t<LAYOUT, GT, false, CAP, 10, kT>(P, sms, s);
+    return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 9, kT>(P, sms, s)
+                 : launch_blocks_t<LAYOUT, GT, false, CAP, 9, kT>(P, sms, s);
+}
+
+#define MDQ_BLOCKS_SIG(NAME, CAP)                                                               \
+    mdq_status launch_blocks_##NAME(int gdt, const LaunchParams<CAP>& P, bool exact, int logb, \
+                                    int sms, cudaStream_t s)
+#define MDQ_BLOCKS_DECLARE(NAME)     \
+    MDQ_BLOCKS_SIG(NAME, kCapSmall); \
+    MDQ_BLOCKS_SIG(NAME, kCapLarge);
+#define MDQ_BLOCKS_DEFINE_CAP(NAME, LAYOUT, CAP)                                                 \
+    MDQ_BLOCKS_SIG(NAME, CAP) {                                                                  \
+        return gdt == MDQ_BF16                                                                   \
+                   ? launch_blocks_mode<LAYOUT, __nv_bfloat16, CAP>(P, exact, logb, sms, s)      \
+                   : launch_blocks_mode<LAYOUT, float, CAP>(P, exact, logb, sms, s);             \
+    }
+#define MDQ_BLOCKS_DEFINE(NAME, LAYOUT)             \
+    MDQ_BLOCKS_DEFINE_CAP(NAME, LAYOUT, kCapSmall)  \
+    MDQ_BLOCKS_DEFINE_CAP(NAME, LAYOUT, kCapLarge)
+
+MDQ_BLOCKS_DECLARE(packed4)
+MDQ_BLOCKS_DECLARE(s8u8)
+MDQ_BLOCKS_DECLARE(s16u16)
+MDQ_BLOCKS_DECLARE(s32u32)
+MDQ_BLOCKS_DECLARE(m8v4)
+
+}  // namespace mdq

@@ -39,6 +39,7 @@
 #include "mdq_codes.cuh"
 
 #include "mdq_tiles.cuh"
+#include "mdq_blocks.cuh"
 
 // The C layout the Python mirror (mdq_b200/kernels.py, _lib.py) packs.
 static_assert(offsetof(mdq_tensor_desc, grad_dtype) == 104, "mdq_tensor_desc layout");
@@ -292,6 +293,37 @@ mdq_status device_sms(int* sms) {
 }
 
 template <int CAP>
+mdq_status launch_blocks(int layout, int gdt, const mdq::LaunchParams<CAP>& P, bool exact, int logb,
+                         int sms, cudaStream_t s) {
+    switch (layout) {
+        case MDQ_LAYOUT_PACKED4: return mdq::launch_blocks_packed4(gdt, P, exact, logb, sms, s);
+        case MDQ_LAYOUT_S8U8: return mdq::launch_blocks_s8u8(gdt, P, exact, logb, sms, s);
+        case MDQ_LAYOUT_S16U16: return mdq::launch_blocks_s16u16(gdt, P, exact, logb, sms, s);
+        case MDQ_LAYOUT_S32U32: return mdq::launch_blocks_s32u32(gdt, P, exact, logb, sms, s);
+        case MDQ_LAYOUT_M8V4: return mdq::launch_blocks_m8v4(gdt, P, exact, logb, sms, s);
+    }
+    return fail(MDQ_ERR_INVALID_ARG, "bad layout %d", layout);
+}
+
+// Which kernel takes a class whose blocks all have 512 or 1024 elements.
+// Measured on B200 (2^30 elements, bf16 gradients, fast p): the tiled kernel
+// is faster for every layout at 1024 (4-bit 434 vs 387, 8-bit 284 vs 204
+// Gparams/s) and for 4-bit fast p at 512; the warp-per-block kernel wins at
+// 512 for 8-bit codes (301 vs 288) and for 4-bit codes in exact p mode (321
+// vs 305).  MDQ_BLOCK_KERNEL=1 selects it for every eligible class
+// (measurement), =0 never; unset: those 512-element cases.  Read once.
+bool use_block_kernel(int layout, int block, bool exact) {
+    static int mode = -2;
+    if (mode == -2) {
+        const char* e = getenv("MDQ_BLOCK_KERNEL");
+        mode = e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
+    }
+    if (mode >= 0) return mode == 1;
+    const bool v4 = layout == MDQ_LAYOUT_PACKED4 || layout == MDQ_LAYOUT_M8V4;
+    return block == 512 && (!v4 || exact);
+}
+
+template <int CAP>
 mdq_status launch_tiles(int layout, int gdt, const mdq::LaunchParams<CAP>& P, bool exact, bool prof,
                         int sms, int pt, int min_block, cudaStream_t s) {
     switch (layout) {
@@ -351,9 +383,39 @@ mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bo
     // 16 elements per thread (4096-element tiles, 2 CTAs per SM) halve the
     // per-tile work; measured on B200 it pays for 4-bit v codes, and for
     // 8-bit codes only with blocks of 1024 or more.
-    int min_block = mdq::kTile;
-    for (int k = 0; k < count; ++k) min_block = std::min(min_block, (int)descs[idx[k]].block);
+    int min_block = mdq::kTile, max_block = 0;
+    for (int k = 0; k < count; ++k) {
+        min_block = std::min(min_block, (int)descs[idx[k]].block);
+        max_block = std::max(max_block, (int)descs[idx[k]].block);
+    }
     const int layout = descs[idx[0]].layout;
+    if (min_block == max_block && (min_block == 512 || min_block == 1024) && prof == nullptr &&
+        use_block_kernel(layout, min_block, exact)) {
+        // Warp-per-block kernel: a launch's units are quantisation blocks.
+        const int logb = min_block == 1024 ? 10 : 9;
+        int i = 0;
+        while (i < count) {
+            P.n_desc = 0;
+            P.prof = nullptr;
+            int64_t units = 0;
+            while (i < count && P.n_desc < CAP) {
+                const mdq_tensor_desc& d = descs[idx[i]];
+                const int64_t u = (d.n + min_block - 1) / min_block;
+                if (units + u > (int64_t)INT32_MAX && P.n_desc > 0) break;
+                mdq::LaunchDesc L = to_launch(d);
+                L.tile_begin = (int32_t)units;
+                P.d[P.n_desc++] = L;
+                units += u;
+                ++i;
+            }
+            P.total_tiles = (int32_t)units;
+            const mdq_tensor_desc& d0 = descs[idx[i - 1]];
+            const mdq_status st = launch_blocks<CAP>(d0.layout, d0.grad_dtype, P, exact, logb,
+                                                     sms, s);
+            if (st != MDQ_OK) return st;
+        }
+        return MDQ_OK;
+    }
     const bool v4 = layout == MDQ_LAYOUT_PACKED4 || layout == MDQ_LAYOUT_M8V4;
     const int pt = MDQ_ENABLE_PT16 && v4 && min_block >= MDQ_V4_PT16_MIN_BLOCK ? 16 : 8;
     const int64_t tile = mdq::kTile;

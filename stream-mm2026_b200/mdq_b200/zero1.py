@@ -568,9 +568,11 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             st["piece"] = (a, n)
 
     # ------------------------------------------------------------------
-    def consolidated_state_dict(self):
-        """The unsharded per-parameter state (reference layout) on every rank:
-        pieces are gathered and concatenated in parameter order."""
+    def consolidated_state_dict(self, dst: Optional[int] = None):
+        """The unsharded per-parameter state (reference layout): pieces are
+        gathered and concatenated in parameter order, on every rank (dst
+        None) or on rank `dst` only (the others return None).  For large
+        models use save_sharded / load_sharded, which gather nothing."""
         local = []
         for pc in self.pieces:
             st = self.state[self.params[pc.param]]
@@ -578,9 +580,15 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             local.append((pc.param, pc.start,
                           {k: (v.detach().cpu().numpy() if torch.is_tensor(v) else v)
                            for k, v in st.items() if k not in ("piece", "_layout_bits")}))
-        if self.world > 1:
+        if self.world > 1 and dst is None:
             everything = [None] * self.world
             dist.all_gather_object(everything, local, group=self.group)
+        elif self.world > 1:
+            everything = [None] * self.world if self.rank == dst else None
+            dist.gather_object(local, everything, dst=dist.get_global_rank(self.group, dst)
+                               if self.group is not None else dst, group=self.group)
+            if self.rank != dst:
+                return None
         else:
             everything = [local]
         by_param = {}
@@ -604,3 +612,136 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
                 "mdq_global_stats": {"n_ema": self.n_ema, "r_ema": self.r_ema,
                                      "v_global_ema": self.v_global_ema,
                                      "total_steps": self.total_steps}}
+
+    # ------------------------------------------------------------------
+    # Sharded checkpoints: every rank writes its own pieces, any world size
+    # reads back the pieces it needs; nothing is gathered.
+    # ------------------------------------------------------------------
+    _CKPT_KEYS = ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min")
+
+    def save_sharded(self, path: str) -> None:
+        """Write this rank's optimizer state to ``path/rank<r>.pt`` and, from
+        rank 0, ``path/manifest.pt`` (world size, block, parameter sizes,
+        hyper-parameters, the policy's global statistics and every
+        parameter's step / bit width / score).  With bf16 parameters each
+        piece's fp32 master parameters are saved too.  Call on every rank."""
+        import os
+
+        os.makedirs(path, exist_ok=True)
+        pieces = {}
+        for pc in self.pieces:
+            st = self.state[self.params[pc.param]]
+            rec = {"start": pc.start, "n": pc.n}
+            for k in self._CKPT_KEYS:
+                rec[k] = st[k].detach().cpu().clone()
+            if self.master is not None:
+                rec["master"] = self._piece_views(pc)[0].detach().cpu().clone()
+            pieces[pc.param] = rec
+        torch.save({"rank": self.rank, "world": self.world, "pieces": pieces},
+                   os.path.join(path, f"rank{self.rank:05d}.pt"))
+        if self.rank == 0:
+            scal = []
+            for p in self.params:
+                st = self.state[p]
+                scal.append({"step": int(st.get("step", 0)),
+                             "current_bit": int(st.get("current_bit", 16)),
+                             "last_score": float(st["last_score"]) if "last_score" in st else 12.0,
+                             "_layout_bits": st.get("_layout_bits")})
+            torch.save({"format": "mdq-zero1-sharded-v1", "world": self.world,
+                        "block": self.block, "numels": list(self.layout.numels),
+                        "param_groups": [{k: v for k, v in g.items() if k != "params"}
+                                         for g in self.param_groups],
+                        "mdq_global_stats": {"n_ema": self.n_ema, "r_ema": self.r_ema,
+                                             "v_global_ema": self.v_global_ema,
+                                             "total_steps": self.total_steps},
+                        "params": scal}, os.path.join(path, "manifest.pt"))
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+    def load_sharded(self, path: str) -> None:
+        """Load a checkpoint written by save_sharded at any world size: each
+        rank memory-maps the saved rank files and copies the slices of codes,
+        scales (and fp32 master parameters) that overlap its own pieces.  The
+        model's parameters are restored by the caller, except that with bf16
+        parameters the fp32 master shards come from the checkpoint when it
+        holds them (and the bf16 parameters are set to their rounding)."""
+        import os
+
+        man = torch.load(os.path.join(path, "manifest.pt"), weights_only=False)
+        if man.get("format") != "mdq-zero1-sharded-v1":
+            raise ValueError(f"{path}: not an MDQ sharded checkpoint")
+        if man["block"] != self.block or man["numels"] != list(self.layout.numels):
+            raise ValueError("checkpoint block size or parameter sizes differ from this optimizer")
+        for g, sg in zip(self.param_groups, man["param_groups"]):
+            for k, v in sg.items():
+                g[k] = v
+        st_g = man["mdq_global_stats"]
+        self.n_ema, self.r_ema = st_g["n_ema"], st_g["r_ema"]
+        self.v_global_ema, self.total_steps = st_g["v_global_ema"], st_g["total_steps"]
+        files = [torch.load(os.path.join(path, f"rank{r:05d}.pt"), mmap=True, weights_only=False)
+                 for r in range(man["world"])]
+        B = self.block
+        self.state.clear()
+        for i, p in enumerate(self.params):
+            sc = man["params"][i]
+            st = self.state[p]
+            st["step"] = sc["step"]
+            st["current_bit"] = sc["current_bit"]
+            st["last_score"] = torch.tensor(sc["last_score"], dtype=torch.float32, device=p.device)
+            if sc["_layout_bits"] is not None:
+                st["_layout_bits"] = sc["_layout_bits"]
+        for pc in self.pieces:
+            p = self.params[pc.param]
+            st = self.state[p]
+            a, n = pc.start, pc.n
+            out = {}
+            for f in files:
+                rec = f["pieces"].get(pc.param)
+                if rec is None:
+                    continue
+                s0, ns = rec["start"], rec["n"]
+                lo, hi = max(a, s0), min(a + n, s0 + ns)
+                if lo >= hi:
+                    continue
+                if (lo - s0) % B or (lo - a) % B:
+                    raise ValueError("piece boundaries are not block-aligned")
+                if not out:
+                    nb = -(-n // B)
+                    easq = rec["exp_avg_sq"]
+                    out["exp_avg"] = torch.empty(n, dtype=rec["exp_avg"].dtype)
+                    if easq.numel() == 0:
+                        out["exp_avg_sq"] = easq.clone()
+                    elif easq.numel() == rec["exp_avg"].numel():
+                        out["exp_avg_sq"] = torch.empty(n, dtype=easq.dtype)
+                    else:
+                        out["exp_avg_sq"] = torch.empty((n + 1) // 2, dtype=easq.dtype)
+                    for k in ("scale_m", "scale_v", "v_min"):
+                        out[k] = torch.empty(nb, dtype=torch.float32)
+                    if "master" in rec:
+                        out["master"] = torch.empty(n, dtype=torch.float32)
+                d0, s_0, m = lo - a, lo - s0, hi - lo
+                out["exp_avg"][d0:d0 + m] = rec["exp_avg"][s_0:s_0 + m]
+                easq = rec["exp_avg_sq"]
+                if easq.numel() == rec["exp_avg"].numel() and easq.numel():
+                    out["exp_avg_sq"][d0:d0 + m] = easq[s_0:s_0 + m]
+                elif easq.numel():
+                    out["exp_avg_sq"][d0 // 2:(d0 + m + 1) // 2] = easq[s_0 // 2:(s_0 + m + 1) // 2]
+                bd, bs, bm = d0 // B, s_0 // B, -(-m // B)
+                for k in ("scale_m", "scale_v", "v_min"):
+                    out[k][bd:bd + bm] = rec[k][bs:bs + bm]
+                if "master" in rec and "master" in out:
+                    out["master"][d0:d0 + m] = rec["master"][s_0:s_0 + m]
+            if not out:
+                continue  # saved before this piece had state
+            for k in self._CKPT_KEYS:
+                st[k] = out[k].to(p.device)
+            st["piece"] = (a, n)
+            if self.master is not None and "master" in out:
+                mv = self._piece_views(pc)[0]
+                mv.copy_(out["master"].to(mv.device))
+                self.flat_param[pc.flat_off:pc.flat_off + n].copy_(mv)
+        del files
+        if self.master is not None and self.world > 1:
+            for k in range(len(self.layout.buckets)):
+                self._all_gather_bucket(k)
+            self.wait_param_gather()
