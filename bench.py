@@ -448,6 +448,48 @@ def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems):
     return out
 
 
+def run_config1(device):
+    """BASELINE config 1 on the GPU, beside the reference arm's CPU timing of
+    the same workload: one fp32 2048 x 2048 tensor, fp32 gradients N(0,
+    1e-3^2) per step, block 2048, 20 steps of (a) MDQAdamWFakeQuant, the
+    reference's pure-PyTorch algorithm fused (fp32 moments), and (b)
+    MDQAdamW, the same constructor with low-bit code state.  Each step()
+    call (host policy included) is timed with CUDA events; median."""
+    import torch
+
+    from mdq_b200 import MDQAdamW, MDQAdamWFakeQuant
+
+    n = CFG1_SHAPE[0] * CFG1_SHAPE[1]
+    out = {}
+    for name, cls in (("fakequant_fp32_moments", MDQAdamWFakeQuant),
+                      ("codes_state", MDQAdamW)):
+        torch.manual_seed(0)
+        p = torch.nn.Parameter((torch.randn(*CFG1_SHAPE) * 0.02).to(device))
+        opt = cls([p], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                  block_size=2048)
+        gen = torch.Generator(device=device).manual_seed(0)
+        grads = [torch.randn(*CFG1_SHAPE, device=device, generator=gen) * 1e-3
+                 for _ in range(20)]
+        times = []
+        for rep in range(2):                      # the first pass warms up
+            for t in range(20):
+                p.grad = grads[t]
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                opt.step()
+                b.record()
+                b.synchronize()
+                if rep:
+                    times.append(a.elapsed_time(b))
+        med = statistics.median(times)
+        out[name] = {"ms_per_step": round(med, 4), "value": round(n / (med * 1e-3) / 1e9, 3),
+                     "unit": UNIT, "bits": int(opt.state[p]["current_bit"])}
+        del opt, p, grads
+    out["what"] = ("config 1 (fp32 2048x2048, block 2048, 20 steps) through optimizer.step() "
+                   "on one B200; median of 20 steps after 20 warm-up steps")
+    return out
+
+
 def nccl_busbw(world, device, nbytes=1 << 30):
     """Bus bandwidth of a plain NCCL all-gather and reduce-scatter of `nbytes`
     (bf16) in this run, the yardstick for the sharded step's collectives."""
@@ -793,6 +835,7 @@ def main() -> int:
             if "zero1_parity" in zero1:
                 line["zero1_parity"] = zero1["zero1_parity"]
         if world == 1 and not args.no_cpu_baseline:
+            line["config1"] = run_config1(torch.device("cuda", local_rank))
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -189,6 +189,43 @@ mdq_status mdq_grad_stats_multi_noalloc(const void* const* grads, const int64_t*
                                         int32_t n_tensors, int32_t grad_dtype, double* out,
                                         cudaStream_t stream);
 
+/*
+ * The reference's pure-PyTorch quantized AdamW (baseline/mdqbock_newhook.py:
+ * MDQAdamW.step, :86-175, with robust_quantize :58-83) as one fused pass per
+ * quantisation block.  That optimizer keeps fp32 moments and updates the
+ * parameters with fake-quantised copies of them:
+ *   m = beta1 m + (1-beta1) g;  v = beta2 v + (1-beta2) g^2       (:159-160)
+ *   m~ = q(m) * s_m,  s_m = (max|m| + 1e-12) / (2^(b-1) - 1),
+ *        q(m) = clamp(rint(m / (s_m + 1e-12)), -2^(b-1), 2^(b-1)-1)     (:78-82)
+ *   v~ = exp(q(v) * s_v + min log(v+1e-12)),  s_v = (max - min of log(v+1e-12))
+ *        / (2^b - 1),  q(v) = clamp(rint((log(v+1e-12) - min) / (s_v + 1e-12)),
+ *        0, 2^b - 1)                                                   (:70-76)
+ *   p *= decay (if apply_decay);  p += step_size * m~ / (sqrt(v~) / sqrt_bc2 + eps)
+ * over blocks of `block` elements, the last one padded with zeros that take
+ * part in the block's extremes (:63-66); bits >= 31 uses m and v unquantised
+ * (:59).  rint is round-half-to-even, as torch.round.  The scalars are the
+ * reference's Python doubles rounded to float, as torch uses them:
+ * one_minus_beta1 = 1 - beta1, decay = 1 - lr * weight_decay, step_size =
+ * -lr / (1 - beta1^step), sqrt_bc2 = sqrt(1 - beta2^step).
+ * No counterpart in the reference's CUDA code.
+ */
+typedef struct mdq_fq_desc {
+    float* p;              /* fp32 [n], updated in place                       */
+    const void* grad;      /* [n], grad_dtype (MDQ_F32 or MDQ_BF16)            */
+    float* exp_avg;        /* fp32 m [n], updated in place                     */
+    float* exp_avg_sq;     /* fp32 v [n], updated in place                     */
+    int64_t n;
+    int32_t block;         /* 1..4096                                          */
+    int32_t bits;          /* 1..32 (>= 31: no quantisation)                   */
+    int32_t grad_dtype;
+    int32_t apply_decay;   /* weight_decay != 0                                */
+    float beta1, one_minus_beta1, beta2, one_minus_beta2;
+    float decay, step_size, sqrt_bc2, eps;
+} mdq_fq_desc;
+
+mdq_status mdq_fakequant_adamw_multi(const mdq_fq_desc* descs, int32_t n_descs,
+                                     cudaStream_t stream);
+
 /* Message describing the calling thread's most recent failure ("" if none). */
 const char* mdq_last_error(void);
 

@@ -57,6 +57,30 @@ class TensorDesc(ctypes.Structure):
     ]
 
 
+class FQDesc(ctypes.Structure):
+    """Mirror of ``mdq_fq_desc``."""
+
+    _fields_ = [
+        ("p", ctypes.c_void_p),
+        ("grad", ctypes.c_void_p),
+        ("exp_avg", ctypes.c_void_p),
+        ("exp_avg_sq", ctypes.c_void_p),
+        ("n", ctypes.c_int64),
+        ("block", ctypes.c_int32),
+        ("bits", ctypes.c_int32),
+        ("grad_dtype", ctypes.c_int32),
+        ("apply_decay", ctypes.c_int32),
+        ("beta1", ctypes.c_float),
+        ("one_minus_beta1", ctypes.c_float),
+        ("beta2", ctypes.c_float),
+        ("one_minus_beta2", ctypes.c_float),
+        ("decay", ctypes.c_float),
+        ("step_size", ctypes.c_float),
+        ("sqrt_bc2", ctypes.c_float),
+        ("eps", ctypes.c_float),
+    ]
+
+
 class StepOptions(ctypes.Structure):
     """Mirror of ``mdq_step_options``."""
 
@@ -96,6 +120,8 @@ _SIGNATURES = {
                                                     ctypes.POINTER(ctypes.c_int64), ctypes.c_int32,
                                                     ctypes.c_int32, ctypes.c_void_p,
                                                     ctypes.c_void_p]),
+    "mdq_fakequant_adamw_multi": (ctypes.c_int, [ctypes.POINTER(FQDesc), ctypes.c_int32,
+                                                 ctypes.c_void_p]),
     "mdq_last_error": (ctypes.c_char_p, []),
     "mdq_abi_version": (ctypes.c_int32, []),
 }

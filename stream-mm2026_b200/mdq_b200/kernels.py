@@ -221,3 +221,43 @@ def layout_for_bits(m_bits: int, v_bits: int) -> int:
 
 __all__ = ["fused_mdq_adamw", "StepItem", "step_multi", "run_descs", "fill_desc", "grad_stats",
            "layout_for_bits", "P_FAST", "P_EXACT", "LAYOUT_NAMES"]
+
+
+def fakequant_step(items, stream: Optional[int] = None) -> None:
+    """Fused step of the reference's pure-PyTorch MDQAdamW
+    (baseline/mdqbock_newhook.py:86-175) for many tensors, on the current
+    stream.  Each item is a dict with p, grad, exp_avg, exp_avg_sq (fp32
+    moments, updated in place), block, bits, and the host-side scalars of
+    the reference's step (beta1, beta2, lr, weight_decay, eps, step)."""
+    import math
+
+    if not items:
+        return
+    arr = (_lib.FQDesc * len(items))()
+    dev = items[0]["p"].device
+    for d, it in zip(arr, items):
+        p, g, m, v = it["p"], it["grad"], it["exp_avg"], it["exp_avg_sq"]
+        for t in (p, g, m, v):
+            _need_cuda(t, "fake-quant step tensors")
+            _need_contig(t, "fake-quant step tensors")
+            if t.numel() != p.numel() or t.device != dev:
+                raise RuntimeError("p, grad, exp_avg, exp_avg_sq must match in size and device")
+        if p.dtype != torch.float32 or m.dtype != torch.float32 or v.dtype != torch.float32:
+            raise RuntimeError("p, exp_avg and exp_avg_sq must be float32")
+        b1, b2, lr, wd, step = (it["beta1"], it["beta2"], it["lr"], it["weight_decay"],
+                                it["step"])
+        bc1, bc2 = 1 - b1 ** step, 1 - b2 ** step
+        d.p, d.grad, d.exp_avg, d.exp_avg_sq = (p.data_ptr(), g.data_ptr(), m.data_ptr(),
+                                                v.data_ptr())
+        d.n, d.block, d.bits = p.numel(), int(it["block"]), int(it["bits"])
+        d.grad_dtype = _DTYPE_CODE.get(g.dtype, -1)
+        d.apply_decay = 1 if wd != 0 else 0
+        d.beta1, d.one_minus_beta1 = b1, 1 - b1
+        d.beta2, d.one_minus_beta2 = b2, 1 - b2
+        d.decay, d.step_size = 1 - lr * wd, -lr / bc1
+        d.sqrt_bc2, d.eps = math.sqrt(bc2), it["eps"]
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.mdq_fakequant_adamw_multi(arr, len(items),
+                                           stream if stream is not None else _stream_handle(dev))
+    _lib.check(st)

@@ -656,10 +656,16 @@ class MDQAdamWSimpleFusedIO(MDQAdamWSimple):
 
 
 class MDQAdamW(MDQAdamWSimpleFusedIO):
-    """Drop-in for ``baseline/mdqbock_newhook.py:MDQAdamW`` as used by
-    ``baseline/pretrain_gpt.py:192-198``: same constructor defaults, state in
-    low-bit codes instead of fp32 moments (``robust_quantize`` and
-    ``quant_error`` come with every class here)."""
+    """Constructor drop-in for ``baseline/mdqbock_newhook.py:MDQAdamW`` as
+    used by ``baseline/pretrain_gpt.py:192-198`` (same defaults, block 2048),
+    but NOT the same algorithm: this class stores m and v as low-bit codes with
+    the CUDA kernel family's semantics (CUDA/stquant_kernel.cu; block clamped
+    to 1024, the FusedIO step counting), while the pure-PyTorch class keeps
+    fp32 moments and only fake-quantises them for the update.  After 20 steps
+    of BASELINE config 1 the two differ by about 7% relative L2 in the
+    parameters.  MDQAdamWFakeQuant reproduces the pure-PyTorch class's
+    algorithm.  (``robust_quantize`` and ``quant_error`` come with every
+    class here.)"""
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  alpha=0.9, layer_count=12, batch_size=8, update_freq=20, block_size=2048,
@@ -667,6 +673,95 @@ class MDQAdamW(MDQAdamWSimpleFusedIO):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                          alpha=alpha, layer_count=layer_count, batch_size=batch_size,
                          update_freq=update_freq, block_size=block_size, **kw)
+
+
+class MDQAdamWFakeQuant(MDQAdamWSimple):
+    """The reference's pure-PyTorch MDQAdamW (baseline/mdqbock_newhook.py:6-184)
+    with the same algorithm: fp32 first and second moments are kept, and each
+    step updates the parameters with block-fake-quantised copies of them
+    (robust_quantize at the tensor's current bit width, blocks of
+    ``block_size`` -- 2048 by default, never clamped).  The score policy,
+    state layout (``exp_avg`` / ``exp_avg_sq`` fp32, ``step``,
+    ``current_bit``, ``last_score``, ``mdq_global_stats``) and checkpoints are
+    the reference's.  What changes is the step: one fused kernel pass
+    (kernels.fakequant_step, ``mdq_fakequant_adamw_multi``) per step for every
+    parameter instead of about twenty torch operations per parameter.  Use
+    this class to keep the reference's training dynamics exactly; MDQAdamW
+    stores the moments as low-bit codes instead (about 1/4 to 1/8 of the
+    optimizer memory) with the CUDA kernel family's semantics."""
+
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                 alpha=0.9, layer_count=12, batch_size=8, update_freq=20, block_size=2048,
+                 *, grad_stats: str = "fused"):
+        super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
+                         alpha=alpha, layer_count=layer_count, batch_size=batch_size,
+                         update_freq=update_freq, block_size=block_size, exact_block=True,
+                         grad_stats=grad_stats)
+
+    def _init_state_if_needed(self, p, state, block_size):
+        """baseline/mdqbock_newhook.py:102-107."""
+        if len(state) != 0:
+            return
+        if p.dtype != torch.float32:
+            raise RuntimeError("MDQ parameters must be float32")
+        state["step"] = 0
+        state["exp_avg"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
+        state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
+        state["current_bit"] = 16
+        state["last_score"] = torch.tensor(12.0, device=p.device)
+
+    def dequantized_moments(self, p):
+        st = self.state[p]
+        return st["exp_avg"].reshape(-1), st["exp_avg_sq"].reshape(-1)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        """baseline/mdqbock_newhook.py:86-175."""
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        self._pending_events = None
+        self.total_steps += 1
+        self.last_step_timings = {k: 0.0 for k in ("mdq_stats_ms", "mdq_bit_decision_ms",
+                                                   "mdq_grad_stats_ms", "mdq_allreduce_ms",
+                                                   "mdq_score_bits_ms")}
+        update_decision = ((self.total_steps % self.param_groups[0]["update_freq"] == 0)
+                           or (self.total_steps < 5))
+        params_with_grad = []
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                params_with_grad.append((p, group))
+                self._init_state_if_needed(p, self.state[p], group["block_size"])
+        if update_decision and params_with_grad:
+            self._decide_bits(params_with_grad)
+        items = []
+        for p, group in params_with_grad:
+            st = self.state[p]
+            st["step"] += 1
+            grad = p.grad if p.grad.is_contiguous() else p.grad.contiguous()
+            items.append(dict(p=p, grad=grad, exp_avg=st["exp_avg"],
+                              exp_avg_sq=st["exp_avg_sq"], block=group["block_size"],
+                              bits=int(st["current_bit"]), beta1=group["betas"][0],
+                              beta2=group["betas"][1], lr=group["lr"],
+                              weight_decay=group["weight_decay"], eps=group["eps"],
+                              step=st["step"]))
+        if items:
+            dev = items[0]["p"].device
+            with torch.cuda.device(dev):
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record()
+                kernels.fakequant_step(items)
+                end.record()
+            self._pending_events = (start, end, None)
+        t = self.last_step_timings
+        for k in ("mdq_unpack_ms", "mdq_pack_ms", "quant_dequant_unpack_ms",
+                  "quant_dequant_pack_ms"):
+            t[k] = 0.0
+        return loss
 
 
 # ----------------------------------------------------------------------
