@@ -61,7 +61,9 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
     float s0 = kNaN, s1 = kNaN, s2 = kNaN;
 
     // ---- pass 1: dequantise, AdamW, parameter update ---------------------
-#pragma unroll
+    // (Sub-tile loops are not unrolled: the unrolled body overflows the
+    // instruction cache, measured as the dominant "no instruction" stall.)
+#pragma unroll 1
     for (int s = 0; s < S; ++s) {
         int cnt[2];
 #pragma unroll
@@ -191,7 +193,7 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
 
     // ---- pass 2: requantise (CUDA/stquant_kernel.cu:204-216) ---------------
     constexpr bool kCorrect = !kApprox;
-#pragma unroll
+#pragma unroll 1
     for (int s = 0; s < S; ++s) {
         float m[8], x[8];
 #pragma unroll
@@ -249,6 +251,13 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
     }
 }
 
+// Partial or unaligned blocks (a tensor's tail) take an out-of-line copy of
+// the body, so the hot loop's code stays small.
+template <int LAYOUT, typename GT, bool EXACT_P, int LOGB, bool TBL>
+__device__ __noinline__ void block_body_tail(const TileCtx& X, int64_t e0, float* wm, float* wx) {
+    block_body<LAYOUT, GT, EXACT_P, false, LOGB, TBL>(X, e0, wm, wx);
+}
+
 // Persistent grid: CTA c takes units [total c / grid, total (c+1) / grid),
 // warp w the units lo + w, lo + w + 8, ...; `tile_begin` of a descriptor
 // counts units (blocks) here.  Each warp stages the tensor it works on in its
@@ -288,7 +297,7 @@ mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
         if (X.vec && e0 + (1 << LOGB) <= X.n)
             block_body<LAYOUT, GT, EXACT_P, true, LOGB, TBL>(X, e0, wm, wx);
         else
-            block_body<LAYOUT, GT, EXACT_P, false, LOGB, TBL>(X, e0, wm, wx);
+            block_body_tail<LAYOUT, GT, EXACT_P, LOGB, TBL>(X, e0, wm, wx);
     }
 }
 
