@@ -618,6 +618,9 @@ def traffic_per_launch(n_elems):
     scaled from its capture size to this launch (traffic is proportional)."""
     lay = "packed4" if BITS == 4 else "s8u8"
     path = os.path.join(REPO, "profiles", f"mdq_step_tiles_{lay}_bf16_b{BLOCK}.json")
+    full = os.path.join(REPO, "profiles", f"mdq_step_tiles_{lay}_bf16_b{BLOCK}_2e{LOG2_N}.json")
+    if os.path.exists(full):
+        path = full          # a capture of this very launch size
     try:
         with open(path) as f:
             d = json.load(f)

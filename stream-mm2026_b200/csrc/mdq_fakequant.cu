@@ -9,9 +9,12 @@
 // gradients (26 with bf16), HBM-bound.
 //
 // Arithmetic follows the torch expression order of the reference, each torch
-// operation rounded once, with the fused multiply-adds torch's own CUDA
-// kernels use for add(alpha=), addcmul and addcdiv; transcendentals are
-// CUDA's logf / expf / sqrtf as torch's CUDA tensors compute them.
+// operation rounded once, with what torch's own CUDA kernels do: fused
+// multiply-adds for add(alpha=), addcmul (value * (t1 * t2) + self) and
+// addcdiv, and a multiplication by the float reciprocal for a tensor divided
+// by a Python number; transcendentals are CUDA's logf / expf / sqrtf as
+// torch's CUDA tensors compute them.  (Each of these was established by
+// comparing candidate expressions with torch's results on a B200.)
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -107,6 +110,7 @@ fq_step(const __grid_constant__ Params P) {
         const int B = d.block;
         const int64_t e0 = (u - D.unit_begin) * (int64_t)B;
         const bool quant = d.bits < 31;
+        const float inv_sqrt_bc2 = __frcp_rn(d.sqrt_bc2);
         const float eps = 1e-12f;
         float m[EPT], v[EPT], lv[EPT];
         float am = 0.0f, lmax = -INFINITY, lmin = INFINITY;
@@ -123,8 +127,9 @@ fq_step(const __grid_constant__ Params P) {
                 const float g = load_g<GT>(d.grad, i);
                 // exp_avg.mul_(beta1).add_(grad, alpha=1-beta1)          (:159)
                 m[k] = __fmaf_rn(d.one_minus_beta1, g, __fmul_rn(__ldcs(d.exp_avg + i), d.beta1));
-                // exp_avg_sq.mul_(beta2).addcmul_(grad, grad, value=1-beta2) (:160)
-                v[k] = __fmaf_rn(__fmul_rn(d.one_minus_beta2, g), g,
+                // exp_avg_sq.mul_(beta2).addcmul_(grad, grad, value=1-beta2) (:160):
+                // torch's CUDA addcmul forms value * (t1 * t2) + self.
+                v[k] = __fmaf_rn(d.one_minus_beta2, __fmul_rn(g, g),
                                  __fmul_rn(__ldcs(d.exp_avg_sq + i), d.beta2));
             }
             // Padding past the end of the tensor is a zero m and v (:63-66).
@@ -142,11 +147,13 @@ fq_step(const __grid_constant__ Params P) {
             cta_extremes(am, lmax, lmin, red);
             const float lm1 = (float)((1 << (d.bits - 1)) - 1);     // q_levels - 1
             const float lv1 = (float)((1u << d.bits) - 1u);         // 2^bits - 1
-            sm = __fdiv_rn(__fadd_rn(am, eps), lm1);                  // (:80)
+            // A tensor divided by a Python number: torch's CUDA kernel multiplies
+            // by the float reciprocal of the number.
+            sm = __fmul_rn(__fadd_rn(am, eps), __frcp_rn(lm1));       // (:80)
             dm = __fadd_rn(sm, eps);
             lo_m = -(float)(1 << (d.bits - 1));
             hi_m = lm1;
-            sv = __fdiv_rn(__fsub_rn(lmax, lmin), lv1);               // (:74)
+            sv = __fmul_rn(__fsub_rn(lmax, lmin), __frcp_rn(lv1));    // (:74)
             dv = __fadd_rn(sv, eps);
             hi_v = lv1;
         }
@@ -168,7 +175,7 @@ fq_step(const __grid_constant__ Params P) {
             float p = d.p[i];
             if (d.apply_decay) p = __fmul_rn(p, d.decay);               // (:168)
             // denom = (q_v.sqrt() / sqrt(bc2)).add_(eps); p.addcdiv_(q_m, denom, value)
-            const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(qv), d.sqrt_bc2), d.eps);
+            const float denom = __fadd_rn(__fmul_rn(__fsqrt_rn(qv), inv_sqrt_bc2), d.eps);
             d.p[i] = __fmaf_rn(d.step_size, __fdiv_rn(qm, denom), p);
             __stcs(d.exp_avg + i, m[k]);
             __stcs(d.exp_avg_sq + i, v[k]);

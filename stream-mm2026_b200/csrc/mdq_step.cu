@@ -306,21 +306,23 @@ mdq_status launch_blocks(int layout, int gdt, const mdq::LaunchParams<CAP>& P, b
 }
 
 // Which kernel takes a class whose blocks all have 512 or 1024 elements.
-// Measured on B200 (2^30 elements, bf16 gradients, fast p): the tiled kernel
-// is faster for every layout at 1024 (4-bit 434 vs 387, 8-bit 284 vs 204
-// Gparams/s) and for 4-bit fast p at 512; the warp-per-block kernel wins at
-// 512 for 8-bit codes (301 vs 288) and for 4-bit codes in exact p mode (321
-// vs 305).  MDQ_BLOCK_KERNEL=1 selects it for every eligible class
-// (measurement), =0 never; unset: those 512-element cases.  Read once.
+// Measured on B200 (2^30 elements, bf16 gradients, Gparams/s, tiled vs
+// warp-per-block, fast p / exact p):
+//   int8/uint8 codes, 1024: 285 vs 291 / 252 vs 266;  512: 289 vs 298 / 255 vs 258
+//   packed 4-bit,     1024: 435 vs 374 / 293 vs 302;  512: 430 vs 369 / 308 vs 288
+// so the warp-per-block kernel takes the int8/uint8 layout and the tiled
+// kernel everything else.  MDQ_BLOCK_KERNEL=1 / =0 forces the choice for
+// every eligible class (measurement).  Read once.
 bool use_block_kernel(int layout, int block, bool exact) {
     static int mode = -2;
     if (mode == -2) {
         const char* e = getenv("MDQ_BLOCK_KERNEL");
         mode = e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
     }
+    (void)block;
+    (void)exact;
     if (mode >= 0) return mode == 1;
-    const bool v4 = layout == MDQ_LAYOUT_PACKED4 || layout == MDQ_LAYOUT_M8V4;
-    return block == 512 && (!v4 || exact);
+    return layout == MDQ_LAYOUT_S8U8;
 }
 
 template <int CAP>

@@ -47,6 +47,11 @@ def test_fakequant_matches_reference_class(cuda_device, sizes, block):
     ref_cls = _reference_class()
     pr, orf, br = _run(ref_cls, sizes, block, 20, cuda_device)
     pm, om, bm = _run(MDQAdamWFakeQuant, sizes, block, 20, cuda_device, grad_stats="reference")
+    diff = {k: sum(int((orf.state[a][k].view(torch.int32) != om.state[b][k].view(torch.int32))
+                       .sum()) for a, b in zip(pr, pm)) for k in ("exp_avg", "exp_avg_sq")}
+    diff["p"] = sum(int((a.detach().view(torch.int32) != b.detach().view(torch.int32)).sum())
+                    for a, b in zip(pr, pm))
+    print(f"sizes {sizes} block {block}: elements differing {diff}")
     assert bm == br
     same = 0
     for a, b in zip(pr, pm):
