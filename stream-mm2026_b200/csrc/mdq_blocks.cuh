@@ -24,6 +24,11 @@
 
 namespace mdq {
 
+// Resident CTAs per SM: 1024-element blocks run 2 (128 registers per thread,
+// no spills, 16 warps), 512-element blocks 3 (80 registers, 24 warps); both
+// measured best on B200 for int8/uint8 codes.
+template <int LOGB> constexpr int blk_min_ctas() { return LOGB >= 10 ? 2 : 3; }
+
 constexpr int kBlkWarps = 8;
 constexpr int kBlkThreads = 32 * kBlkWarps;
 
@@ -32,10 +37,53 @@ template <int LOGB> constexpr int blocks_smem_bytes() {
     return kBlkWarps * (2 << LOGB) * (int)sizeof(float);
 }
 
+// Raw (undecoded) gradient words of 4 elements, so that a sub-tile's loads
+// can be issued one sub-tile ahead and decoded later.
+template <typename GT> struct GradRaw;
+template <> struct GradRaw<float> {
+    using T = float4;
+    __device__ static T load(const void* g, int64_t e) {
+        return __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(g) + e));
+    }
+    __device__ static void decode(const T& w, float* o) { o[0] = w.x; o[1] = w.y; o[2] = w.z; o[3] = w.w; }
+};
+template <> struct GradRaw<__nv_bfloat16> {
+    using T = uint2;
+    __device__ static T load(const void* g, int64_t e) {
+        return __ldcs(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(g) + e));
+    }
+    __device__ static void decode(const T& w, float* o) {
+        o[0] = __uint_as_float(w.x << 16);
+        o[1] = __uint_as_float(w.x & 0xffff0000u);
+        o[2] = __uint_as_float(w.y << 16);
+        o[3] = __uint_as_float(w.y & 0xffff0000u);
+    }
+};
+
+// Loads of one sub-tile (int8/uint8 codes), issued ahead of their use.
+template <typename GT> struct PreLoads {
+    float4 p[2];
+    typename GradRaw<GT>::T g[2];
+    unsigned m[2], v[2];
+    bool valid;
+    __device__ void load(const TensorPtrs& T, int64_t e_sub, int lane) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int64_t e = e_sub + 128 * i + 4 * lane;
+            p[i] = __ldcs(reinterpret_cast<const float4*>(T.p + e));
+            g[i] = GradRaw<GT>::load(T.g, e);
+            m[i] = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const int8_t*>(T.m) + e));
+            v[i] = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(T.v) + e));
+        }
+        valid = true;
+    }
+};
+
 // One quantisation block (unit) of the tensor in X, starting at element e0.
 // FULL: all B elements in range and all pointers allow vector access.
 template <int LAYOUT, typename GT, bool EXACT_P, bool FULL, int LOGB, bool TBL>
-__device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* wm, float* wx) {
+__device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* wm, float* wx,
+                                           PreLoads<GT>& pre, int64_t next_e0) {
     using CI = Codes<LAYOUT>;
     using TC = TableCodes<LAYOUT>;
     constexpr int B = 1 << LOGB;
@@ -63,6 +111,13 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
     // ---- pass 1: dequantise, AdamW, parameter update ---------------------
     // (Sub-tile loops are not unrolled: the unrolled body overflows the
     // instruction cache, measured as the dominant "no instruction" stall.)
+    // int8/uint8 codes, full blocks: one sub-tile of loads in flight ahead;
+    // during the last sub-tile, the first sub-tile of the warp's next block
+    // (next_e0 >= 0: same tensor, full) is loaded.
+    constexpr bool kPre = FULL && LAYOUT == MDQ_LAYOUT_S8U8;
+    if constexpr (kPre) {
+        if (!pre.valid) pre.load(T, e0, lane);
+    }
 #pragma unroll 1
     for (int s = 0; s < S; ++s) {
         int cnt[2];
@@ -77,33 +132,54 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
         float p[8], g[8], m[8], v[8];
         int qm[8], qv[8];
         typename TC::Raw raw[2];
+        if constexpr (kPre) {
+            // Decode the words loaded during the previous sub-tile, then
+            // issue the next sub-tile's loads so they fly during this one.
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
-            if (FULL) {
-                const float4 a = __ldcs(reinterpret_cast<const float4*>(T.p + e));
-                p[4 * i + 0] = a.x; p[4 * i + 1] = a.y; p[4 * i + 2] = a.z; p[4 * i + 3] = a.w;
-                float gg[4];
-                Grad<GT>::load4(T.g, e, gg);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) g[4 * i + j] = gg[j];
-                if constexpr (kTab) {
-                    TC::load4(T, e, raw[i]);
-                } else {
-                    int am[4], av[4];
-                    CI::load4(T, e, am, av);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) { qm[4 * i + j] = am[j]; qv[4 * i + j] = av[j]; }
-                }
-            } else {
+            for (int i = 0; i < 2; ++i) {
+                p[4 * i + 0] = pre.p[i].x; p[4 * i + 1] = pre.p[i].y;
+                p[4 * i + 2] = pre.p[i].z; p[4 * i + 3] = pre.p[i].w;
+                GradRaw<GT>::decode(pre.g[i], g + 4 * i);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const int k = 4 * i + j;
-                    p[k] = 0.0f; g[k] = 0.0f; qm[k] = 0; qv[k] = 0;
-                    if (j < cnt[i]) {
-                        p[k] = T.p[e + j];
-                        g[k] = Grad<GT>::load1(T.g, e + j);
-                        CI::load1(T, e + j, qm[k], qv[k]);
+                    qm[4 * i + j] = (int)(int8_t)(uint8_t)(pre.m[i] >> (8 * j));
+                    qv[4 * i + j] = (int)((pre.v[i] >> (8 * j)) & 0xffu);
+                }
+            }
+            pre.valid = false;
+            if (s + 1 < S)
+                pre.load(T, e0 + 256 * (s + 1), lane);
+            else if (next_e0 >= 0)
+                pre.load(T, next_e0, lane);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
+                if (FULL) {
+                    const float4 a = __ldcs(reinterpret_cast<const float4*>(T.p + e));
+                    p[4 * i + 0] = a.x; p[4 * i + 1] = a.y; p[4 * i + 2] = a.z; p[4 * i + 3] = a.w;
+                    float gg[4];
+                    Grad<GT>::load4(T.g, e, gg);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) g[4 * i + j] = gg[j];
+                    if constexpr (kTab) {
+                        TC::load4(T, e, raw[i]);
+                    } else {
+                        int am[4], av[4];
+                        CI::load4(T, e, am, av);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) { qm[4 * i + j] = am[j]; qv[4 * i + j] = av[j]; }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int k = 4 * i + j;
+                        p[k] = 0.0f; g[k] = 0.0f; qm[k] = 0; qv[k] = 0;
+                        if (j < cnt[i]) {
+                            p[k] = T.p[e + j];
+                            g[k] = Grad<GT>::load1(T.g, e + j);
+                            CI::load1(T, e + j, qm[k], qv[k]);
+                        }
                     }
                 }
             }
@@ -255,7 +331,9 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
 // the body, so the hot loop's code stays small.
 template <int LAYOUT, typename GT, bool EXACT_P, int LOGB, bool TBL>
 __device__ __noinline__ void block_body_tail(const TileCtx& X, int64_t e0, float* wm, float* wx) {
-    block_body<LAYOUT, GT, EXACT_P, false, LOGB, TBL>(X, e0, wm, wx);
+    PreLoads<GT> none;
+    none.valid = false;
+    block_body<LAYOUT, GT, EXACT_P, false, LOGB, TBL>(X, e0, wm, wx, none, -1);
 }
 
 // Persistent grid: CTA c takes units [total c / grid, total (c+1) / grid),
@@ -263,7 +341,7 @@ __device__ __noinline__ void block_body_tail(const TileCtx& X, int64_t e0, float
 // counts units (blocks) here.  Each warp stages the tensor it works on in its
 // own shared-memory slot.
 template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL>
-__global__ void __launch_bounds__(kBlkThreads, 3)
+__global__ void __launch_bounds__(kBlkThreads, blk_min_ctas<LOGB>())
 mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
     extern __shared__ __align__(16) float s_park[];
     __shared__ TileCtx s_wctx[kBlkWarps];
@@ -276,8 +354,11 @@ mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
     const int lo = (int)(total * blockIdx.x / gridDim.x);
     const int hi = (int)(total * (blockIdx.x + 1) / gridDim.x);
     int cur_end = -1;
+    PreLoads<GT> pre;
+    pre.valid = false;
     for (int u = lo + w; u < hi; u += kBlkWarps) {
         if (u >= cur_end) {
+            pre.valid = false;
             __syncwarp();
             if (lane == 0) {
                 const LaunchDesc& D = P.d[find_desc(P, u)];
@@ -294,10 +375,16 @@ mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
             cur_end = X.tile_end;
         }
         const int64_t e0 = (int64_t)(u - X.tile_begin) << LOGB;
-        if (X.vec && e0 + (1 << LOGB) <= X.n)
-            block_body<LAYOUT, GT, EXACT_P, true, LOGB, TBL>(X, e0, wm, wx);
-        else
+        if (X.vec && e0 + (1 << LOGB) <= X.n) {
+            // The warp's next block, when it is a full block of this tensor.
+            const int u2 = u + kBlkWarps;
+            const int64_t e2 = (int64_t)(u2 - X.tile_begin) << LOGB;
+            const int64_t next_e0 = (u2 < hi && u2 < cur_end && e2 + (1 << LOGB) <= X.n) ? e2 : -1;
+            block_body<LAYOUT, GT, EXACT_P, true, LOGB, TBL>(X, e0, wm, wx, pre, next_e0);
+        } else {
+            pre.valid = false;
             block_body_tail<LAYOUT, GT, EXACT_P, LOGB, TBL>(X, e0, wm, wx);
+        }
     }
 }
 
