@@ -60,7 +60,9 @@ template <> struct GradRaw<__nv_bfloat16> {
     }
 };
 
-// Loads of one sub-tile (int8/uint8 codes), issued ahead of their use.
+// Loads of one sub-tile, issued ahead of their use: p, g and the code words
+// (one byte per element of m codes or of packed 4-bit pairs, and of v codes
+// when the layout has a separate v array).
 template <typename GT> struct PreLoads {
     float4 p[2];
     typename GradRaw<GT>::T g[2];
@@ -72,8 +74,9 @@ template <typename GT> struct PreLoads {
             const int64_t e = e_sub + 128 * i + 4 * lane;
             p[i] = __ldcs(reinterpret_cast<const float4*>(T.p + e));
             g[i] = GradRaw<GT>::load(T.g, e);
-            m[i] = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const int8_t*>(T.m) + e));
-            v[i] = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(T.v) + e));
+            m[i] = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(T.m) + e));
+            if (T.v != nullptr)
+                v[i] = __ldcs(reinterpret_cast<const unsigned*>(static_cast<const uint8_t*>(T.v) + e));
         }
         valid = true;
     }
@@ -114,7 +117,8 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
     // int8/uint8 codes, full blocks: one sub-tile of loads in flight ahead;
     // during the last sub-tile, the first sub-tile of the warp's next block
     // (next_e0 >= 0: same tensor, full) is loaded.
-    constexpr bool kPre = FULL && LAYOUT == MDQ_LAYOUT_S8U8;
+    constexpr bool kPre = FULL && (LAYOUT == MDQ_LAYOUT_S8U8 ||
+                                   (LAYOUT == MDQ_LAYOUT_PACKED4 && kTab));
     if constexpr (kPre) {
         if (!pre.valid) pre.load(T, e0, lane);
     }
@@ -140,10 +144,14 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                 p[4 * i + 0] = pre.p[i].x; p[4 * i + 1] = pre.p[i].y;
                 p[4 * i + 2] = pre.p[i].z; p[4 * i + 3] = pre.p[i].w;
                 GradRaw<GT>::decode(pre.g[i], g + 4 * i);
+                if constexpr (LAYOUT == MDQ_LAYOUT_PACKED4) {
+                    raw[i].w = pre.m[i];   // the packed byte pairs, decoded by table
+                } else {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    qm[4 * i + j] = (int)(int8_t)(uint8_t)(pre.m[i] >> (8 * j));
-                    qv[4 * i + j] = (int)((pre.v[i] >> (8 * j)) & 0xffu);
+                    for (int j = 0; j < 4; ++j) {
+                        qm[4 * i + j] = (int)(int8_t)(uint8_t)(pre.m[i] >> (8 * j));
+                        qv[4 * i + j] = (int)((pre.v[i] >> (8 * j)) & 0xffu);
+                    }
                 }
             }
             pre.valid = false;
