@@ -308,21 +308,20 @@ mdq_status launch_blocks(int layout, int gdt, const mdq::LaunchParams<CAP>& P, b
 // Which kernel takes a class whose blocks all have 512 or 1024 elements.
 // Measured on B200 (2^30 elements, bf16 gradients, Gparams/s, tiled vs
 // warp-per-block, fast p / exact p):
-//   int8/uint8 codes, 1024: 285 vs 291 / 252 vs 266;  512: 289 vs 298 / 255 vs 258
-//   packed 4-bit,     1024: 435 vs 374 / 293 vs 302;  512: 430 vs 369 / 308 vs 288
-// so the warp-per-block kernel takes the int8/uint8 layout and the tiled
-// kernel everything else.  MDQ_BLOCK_KERNEL=1 / =0 forces the choice for
-// every eligible class (measurement).  Read once.
+//   int8/uint8 codes, 1024: 285 vs 316-322 / 252 vs 286-292
+//   packed 4-bit,     1024: 435 vs 402 / 293 vs 329
+// so the warp-per-block kernel takes the int8/uint8 layout, and packed 4-bit
+// codes in exact p mode at 1024-element blocks; the tiled kernel the rest.
+// MDQ_BLOCK_KERNEL=1 / =0 forces the choice for every eligible class
+// (measurement).  Read once.
 bool use_block_kernel(int layout, int block, bool exact) {
     static int mode = -2;
     if (mode == -2) {
         const char* e = getenv("MDQ_BLOCK_KERNEL");
         mode = e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
     }
-    (void)block;
-    (void)exact;
     if (mode >= 0) return mode == 1;
-    return layout == MDQ_LAYOUT_S8U8;
+    return layout == MDQ_LAYOUT_S8U8 || (layout == MDQ_LAYOUT_PACKED4 && exact && block == 1024);
 }
 
 template <int CAP>
