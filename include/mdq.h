@@ -200,13 +200,15 @@ mdq_status mdq_grad_stats_multi_noalloc(const void* const* grads, const int64_t*
  *   v~ = exp(q(v) * s_v + min log(v+1e-12)),  s_v = (max - min of log(v+1e-12))
  *        / (2^b - 1),  q(v) = clamp(rint((log(v+1e-12) - min) / (s_v + 1e-12)),
  *        0, 2^b - 1)                                                   (:70-76)
- *   p *= decay (if apply_decay);  p += step_size * m~ / (sqrt(v~) / sqrt_bc2 + eps)
+ *   p *= decay (if apply_decay);  p += step_size * m~ / (sqrt(v~) * inv_sqrt_bc2 + eps)
  * over blocks of `block` elements, the last one padded with zeros that take
  * part in the block's extremes (:63-66); bits >= 31 uses m and v unquantised
  * (:59).  rint is round-half-to-even, as torch.round.  The scalars are the
  * reference's Python doubles rounded to float, as torch uses them:
  * one_minus_beta1 = 1 - beta1, decay = 1 - lr * weight_decay, step_size =
- * -lr / (1 - beta1^step), sqrt_bc2 = sqrt(1 - beta2^step).
+ * -lr / (1 - beta1^step), inv_sqrt_bc2 = 1 / sqrt(1 - beta2^step) (torch
+ * divides a tensor by a Python number by multiplying with the reciprocal,
+ * computed in double and rounded to float).
  * No counterpart in the reference's CUDA code.
  */
 typedef struct mdq_fq_desc {
@@ -220,7 +222,7 @@ typedef struct mdq_fq_desc {
     int32_t grad_dtype;
     int32_t apply_decay;   /* weight_decay != 0                                */
     float beta1, one_minus_beta1, beta2, one_minus_beta2;
-    float decay, step_size, sqrt_bc2, eps;
+    float decay, step_size, inv_sqrt_bc2, eps;
 } mdq_fq_desc;
 
 mdq_status mdq_fakequant_adamw_multi(const mdq_fq_desc* descs, int32_t n_descs,

@@ -11,8 +11,8 @@
 // Arithmetic follows the torch expression order of the reference, each torch
 // operation rounded once, with what torch's own CUDA kernels do: fused
 // multiply-adds for add(alpha=), addcmul (value * (t1 * t2) + self) and
-// addcdiv, and a multiplication by the float reciprocal for a tensor divided
-// by a Python number; transcendentals are CUDA's logf / expf / sqrtf as
+// addcdiv, and a multiplication by the reciprocal (computed in double,
+// rounded to float) for a tensor divided by a Python number; transcendentals are CUDA's logf / expf / sqrtf as
 // torch's CUDA tensors compute them.  (Each of these was established by
 // comparing candidate expressions with torch's results on a B200.)
 #include <cuda_runtime.h>
@@ -110,7 +110,6 @@ fq_step(const __grid_constant__ Params P) {
         const int B = d.block;
         const int64_t e0 = (u - D.unit_begin) * (int64_t)B;
         const bool quant = d.bits < 31;
-        const float inv_sqrt_bc2 = __frcp_rn(d.sqrt_bc2);
         const float eps = 1e-12f;
         float m[EPT], v[EPT], lv[EPT];
         float am = 0.0f, lmax = -INFINITY, lmin = INFINITY;
@@ -148,12 +147,12 @@ fq_step(const __grid_constant__ Params P) {
             const float lm1 = (float)((1 << (d.bits - 1)) - 1);     // q_levels - 1
             const float lv1 = (float)((1u << d.bits) - 1u);         // 2^bits - 1
             // A tensor divided by a Python number: torch's CUDA kernel multiplies
-            // by the float reciprocal of the number.
-            sm = __fmul_rn(__fadd_rn(am, eps), __frcp_rn(lm1));       // (:80)
+            // by the reciprocal of the number, computed in double, as a float.
+            sm = __fmul_rn(__fadd_rn(am, eps), (float)(1.0 / (double)lm1));  // (:80)
             dm = __fadd_rn(sm, eps);
             lo_m = -(float)(1 << (d.bits - 1));
             hi_m = lm1;
-            sv = __fmul_rn(__fsub_rn(lmax, lmin), __frcp_rn(lv1));    // (:74)
+            sv = __fmul_rn(__fsub_rn(lmax, lmin), (float)(1.0 / (double)lv1));  // (:74)
             dv = __fadd_rn(sv, eps);
             hi_v = lv1;
         }
@@ -175,7 +174,7 @@ fq_step(const __grid_constant__ Params P) {
             float p = d.p[i];
             if (d.apply_decay) p = __fmul_rn(p, d.decay);               // (:168)
             // denom = (q_v.sqrt() / sqrt(bc2)).add_(eps); p.addcdiv_(q_m, denom, value)
-            const float denom = __fadd_rn(__fmul_rn(__fsqrt_rn(qv), inv_sqrt_bc2), d.eps);
+            const float denom = __fadd_rn(__fmul_rn(__fsqrt_rn(qv), d.inv_sqrt_bc2), d.eps);
             d.p[i] = __fmaf_rn(d.step_size, __fdiv_rn(qm, denom), p);
             __stcs(d.exp_avg + i, m[k]);
             __stcs(d.exp_avg_sq + i, v[k]);

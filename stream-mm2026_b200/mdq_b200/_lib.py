@@ -76,7 +76,7 @@ class FQDesc(ctypes.Structure):
         ("one_minus_beta2", ctypes.c_float),
         ("decay", ctypes.c_float),
         ("step_size", ctypes.c_float),
-        ("sqrt_bc2", ctypes.c_float),
+        ("inv_sqrt_bc2", ctypes.c_float),
         ("eps", ctypes.c_float),
     ]
 

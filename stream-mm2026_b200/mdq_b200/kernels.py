@@ -255,7 +255,7 @@ def fakequant_step(items, stream: Optional[int] = None) -> None:
         d.beta1, d.one_minus_beta1 = b1, 1 - b1
         d.beta2, d.one_minus_beta2 = b2, 1 - b2
         d.decay, d.step_size = 1 - lr * wd, -lr / bc1
-        d.sqrt_bc2, d.eps = math.sqrt(bc2), it["eps"]
+        d.inv_sqrt_bc2, d.eps = 1.0 / math.sqrt(bc2), it["eps"]
     lib = _lib.load()
     with torch.cuda.device(dev):
         st = lib.mdq_fakequant_adamw_multi(arr, len(items),

@@ -4,10 +4,8 @@ both on the GPU from the same seeded state and gradients.
 
 The reference class runs its torch operations on CUDA tensors; ours runs one
 fused kernel (mdq_fakequant_adamw_multi).  Required after 20 steps: the same
-bit widths chosen at every step, the fp32 moments bit-identical (their update
-involves no quantisation), and the parameters within 1e-6 relative L2 and
-1e-6 of max|p| (the task's parameter tolerance); the test also prints how many
-parameters are bit-identical.
+bit widths chosen at every step, and the fp32 moments and the parameters
+bit-identical.
 """
 import pytest
 import torch
@@ -59,10 +57,8 @@ def test_fakequant_matches_reference_class(cuda_device, sizes, block):
         assert sa["step"] == sb["step"]
         for k in ("exp_avg", "exp_avg_sq"):
             assert torch.equal(sa[k].view(torch.int32), sb[k].view(torch.int32)), k
-        d = (a.detach() - b.detach()).double()
-        assert d.abs().max().item() <= 1e-6 * a.detach().abs().max().item()
-        assert (d.norm() / a.detach().double().norm()).item() <= 1e-6
         same += int((a.detach().view(torch.int32) == b.detach().view(torch.int32)).sum())
+        assert torch.equal(a.detach().view(torch.int32), b.detach().view(torch.int32))
     total = sum(sizes)
     print(f"sizes {sizes} block {block}: bits {sorted({x for r in br for x in r})}, "
           f"parameters bit-identical {same}/{total}")
