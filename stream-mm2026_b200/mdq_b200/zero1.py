@@ -525,7 +525,10 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         """Load an unsharded state (from ``consolidated_state_dict``, at any
         world size, or from an unsharded MDQ optimizer's ``state_dict``): each
         rank keeps the slices of codes and scales that fall in its pieces.
-        Parameters themselves are restored by the caller (model state)."""
+        Parameters themselves are restored by the caller (model state), except
+        that with bf16 parameters the fp32 master shards are restored from the
+        state's "master" entries when present (and the bf16 parameters set to
+        their rounding and gathered)."""
         saved = state_dict["state"]
         for g, sg in zip(self.param_groups, state_dict["param_groups"]):
             for k, v in sg.items():
@@ -566,6 +569,14 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             for k in ("scale_m", "scale_v", "v_min"):
                 st[k] = src[k][b0:b0 + nb].to(p.device, torch.float32, copy=True)
             st["piece"] = (a, n)
+            if self.master is not None and "master" in src:
+                mv = self._piece_views(pc)[0]
+                mv.copy_(src["master"][a:a + n].to(mv.device))
+                self.flat_param[pc.flat_off:pc.flat_off + n].copy_(mv)
+        if self.master is not None and self.world > 1:
+            for k in range(len(self.layout.buckets)):
+                self._all_gather_bucket(k)
+            self.wait_param_gather()
 
     # ------------------------------------------------------------------
     def consolidated_state_dict(self, dst: Optional[int] = None):
@@ -577,9 +588,11 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         for pc in self.pieces:
             st = self.state[self.params[pc.param]]
             # Transported as numpy: torch's object pickling mishandles uint16/32.
-            local.append((pc.param, pc.start,
-                          {k: (v.detach().cpu().numpy() if torch.is_tensor(v) else v)
-                           for k, v in st.items() if k not in ("piece", "_layout_bits")}))
+            rec = {k: (v.detach().cpu().numpy() if torch.is_tensor(v) else v)
+                   for k, v in st.items() if k not in ("piece", "_layout_bits")}
+            if self.master is not None:
+                rec["master"] = self._piece_views(pc)[0].detach().cpu().numpy()
+            local.append((pc.param, pc.start, rec))
         if self.world > 1 and dst is None:
             everything = [None] * self.world
             dist.all_gather_object(everything, local, group=self.group)
@@ -605,6 +618,10 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
                 ts = [st[k] for _, st in parts if st[k].numel() or k != "exp_avg_sq"]
                 full[k] = torch.cat(ts) if ts else first[k]
+            if "master" in first:
+                # bf16 parameters: the fp32 master weights (not part of the
+                # reference's layout; load_consolidated_state_dict restores them)
+                full["master"] = torch.cat([st["master"] for _, st in parts])
             state[i] = full
         return {"state": state,
                 "param_groups": [{k: v for k, v in g.items() if k != "params"}

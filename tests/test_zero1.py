@@ -515,3 +515,80 @@ def test_sharded_checkpoint_1e8_elements_2_to_3_ranks(tmp_path):
             assert torch.equal(t.view(torch.uint8), full_b[i][k].view(torch.uint8)), (i, k)
     # the state is not trivial: the step moved the scales off their initial values
     assert not torch.equal(full_a[0]["v_min"], torch.full_like(full_a[0]["v_min"], -20.0))
+
+
+def _bf16_resume_worker(rank, world, port, sizes, phase, payload, q):
+    """bf16 parameters: phase "save" runs steps 1-3 and returns the
+    consolidated state (with fp32 masters); phase "resume" loads it at this
+    world size and runs steps 4-6.  Gradients are every rank's average."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _use_oracle()
+        from mdq_b200.zero1 import ZeroMDQAdamW
+
+        torch.set_num_threads(1)
+        params = _params(sizes)
+        opt = ZeroMDQAdamW(params, lr=1e-3, weight_decay=0.01, block_size=256, fixed_bits=(8, 4),
+                           param_dtype=torch.bfloat16, bucket_elems=3000)
+        steps = range(1, 4)
+        if phase == "resume":
+            opt.load_consolidated_state_dict(_torch_tree(payload))
+            steps = range(4, 7)
+        for t in steps:
+            opt.zero_grad()
+            avg = [sum(gs) / 2 for gs in zip(*[_bf16_grads(r, t, sizes) for r in range(2)])]
+            for p, g in zip(params, avg):
+                p.grad.copy_(g.to(torch.bfloat16))
+            opt.step()
+        sd = opt.consolidated_state_dict(dst=0)
+        if rank == 0:
+            q.put((_np_tree(sd), [p.detach().float().numpy().copy() for p in params]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bf16_consolidated_resume_restores_masters():
+    """The consolidated state of a bf16-parameter run carries the fp32
+    masters: resumed at another world size, 3 + 3 steps equal 6 unsharded
+    fp32 steps bit for bit (masters), and the parameters are their bf16."""
+    sizes = SIZES
+    _use_oracle()
+    from mdq_b200.optim import MDQAdamWSimpleFusedIO
+
+    torch.set_num_threads(1)
+    ref = _params(sizes)
+    ref_opt = MDQAdamWSimpleFusedIO(ref, lr=1e-3, weight_decay=0.01, block_size=256,
+                                    fixed_bits=(8, 4))
+    for t in range(1, 7):
+        avg = [sum(gs) / 2 for gs in zip(*[_bf16_grads(r, t, sizes) for r in range(2)])]
+        for p, g in zip(ref, avg):
+            p.grad_dtype = torch.bfloat16
+            p.grad = g.to(torch.bfloat16)
+        ref_opt.step()
+
+    def spawn(world, phase, payload):
+        ctx = mp.get_context("spawn")
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_bf16_resume_worker,
+                             args=(r, world, port, sizes, phase, payload, q)) for r in range(world)]
+        for p in procs:
+            p.start()
+        out = q.get(timeout=300)
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        return out
+
+    saved, _ = spawn(2, "save", None)
+    sd, model = spawn(3, "resume", saved)
+    sd = _torch_tree(sd)
+    for i, p in enumerate(ref):
+        want = p.detach()
+        assert torch.equal(sd["state"][i]["master"].view(torch.int32), want.view(torch.int32)), i
+        np.testing.assert_array_equal(model[i], want.to(torch.bfloat16).float().numpy())
+        for k in ("exp_avg", "exp_avg_sq", "scale_m", "scale_v", "v_min"):
+            np.testing.assert_array_equal(ref_opt.state[p][k].numpy().view(np.uint8),
+                                          sd["state"][i][k].numpy().view(np.uint8))
