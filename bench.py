@@ -424,7 +424,7 @@ def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems):
     a.record()
     for _ in range(steps):
         opt.step()
-        phases.append(opt._phase_events)
+        phases.append(opt.phase_events)
     b.record()
     torch.cuda.synchronize()
     total_ms = a.elapsed_time(b) / steps

@@ -374,6 +374,13 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
                         self._wait_bucket(k)
                 self._module_hooks.append(mod.register_forward_pre_hook(pre_hook))
 
+    @property
+    def phase_events(self):
+        """The latest step's four CUDA events (start, after the reduce-scatter,
+        after the step kernels, end) with ``profile_phases``, else None; read
+        them after the timed region to avoid a synchronisation per step."""
+        return self._phase_events
+
     def last_phase_ms(self):
         """Device time of the latest step's phases (``profile_phases``):
         reduce_scatter (waiting for the gradient reduce-scatters), step (the
