@@ -391,7 +391,7 @@ def _max_over_ranks(x, device, world):
     return t.tolist()
 
 
-def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems):
+def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems, param_gather="nccl"):
     """One ZeroMDQAdamW.step() of a fixed model on N GPUs (strong scaling:
     the model is the same at every N): bf16 gradients reduce-scattered over
     NCCL, the fused step on each rank's shard, parameters all-gathered.  The
@@ -410,7 +410,8 @@ def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems):
     n = sum(p.numel() for p in params)
     opt = ZeroMDQAdamW(params, lr=1e-3, weight_decay=0.01, block_size=spec["block"],
                        fixed_bits=spec["bits"], p_mode="fast", grad_dtype=torch.bfloat16,
-                       param_dtype=param_dtype, bucket_elems=bucket_elems, profile_phases=True)
+                       param_dtype=param_dtype, bucket_elems=bucket_elems, profile_phases=True,
+                       param_gather=param_gather)
     del params
     opt.flat_grad.normal_(0, 1e-3, generator=torch.Generator(device=device).manual_seed(rank))
     for _ in range(3):
@@ -445,6 +446,8 @@ def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems):
            "bits": spec["bits"], "block": spec["block"], "grad_dtype": "bf16",
            "param_dtype": "fp32" if param_dtype == torch.float32 else "bf16 (fp32 master shard)",
            "buckets": len(opt.layout.buckets), "steps": steps,
+           "param_gather": ("step kernel stores into every rank's copy (symmetric memory, NVLink)"
+                            if param_gather == "peer" else "NCCL all-gather per bucket"),
            "ms_per_step": round(total_ms, 3),
            "gparams_per_s": round(n / (total_ms * 1e-3) / 1e9, 2),
            "phases_ms": {"reduce_scatter": round(rs_ms, 3), "step": round(step_ms, 3),
@@ -550,7 +553,9 @@ def zero1_parity(world, rank, device):
     identical, for fixed 4-bit, fixed (8, 4) and the score policy, exact p,
     fp32 parameters; and for bf16 parameters (fp32 master) the master must
     equal the unsharded parameters and the gathered bf16 parameters their
-    rounding.  Returns True only if every rank agrees."""
+    rounding.  Two cases gather through the step kernel's own stores into
+    symmetric memory (param_gather="peer").  Returns True only if every rank
+    agrees."""
     import torch
     import torch.distributed as dist
 
@@ -575,15 +580,24 @@ def zero1_parity(world, rank, device):
                 for n in sizes]
 
     ok = True
-    for kw, pdt in ((dict(fixed_bits=4), torch.float32), (dict(fixed_bits=(8, 4)), torch.float32),
-                    (dict(), torch.float32), (dict(fixed_bits=4), torch.bfloat16)):
+    for kw, pdt, gather in ((dict(fixed_bits=4), torch.float32, "nccl"),
+                            (dict(fixed_bits=(8, 4)), torch.float32, "nccl"),
+                            (dict(), torch.float32, "nccl"),
+                            (dict(fixed_bits=4), torch.bfloat16, "nccl"),
+                            (dict(fixed_bits=(8, 4)), torch.float32, "peer"),
+                            (dict(fixed_bits=4), torch.bfloat16, "peer")):
         common = dict(lr=1e-3, weight_decay=0.01, block_size=256, p_mode="exact", **kw)
         ref = params()
         ref_opt = MDQAdamWSimpleFusedIO(ref, **common)
         mine = params()
-        opt = ZeroMDQAdamW(mine, bucket_elems=400_000, param_dtype=pdt,
-                           grad_dtype=torch.bfloat16 if pdt == torch.bfloat16 else torch.float32,
-                           **common)
+        try:
+            opt = ZeroMDQAdamW(mine, bucket_elems=400_000, param_dtype=pdt,
+                               grad_dtype=torch.bfloat16 if pdt == torch.bfloat16 else torch.float32,
+                               param_gather=gather, **common)
+        except (RuntimeError, ValueError):
+            if gather == "peer":      # no symmetric memory on this box: nothing to check
+                continue
+            raise
         for t in range(1, 6):
             per = [grads(r, t, pdt == torch.bfloat16) for r in range(world)]
             opt.zero_grad()
@@ -822,6 +836,14 @@ def main() -> int:
             if world > 1:
                 zero1["runs"].append(run_sharded(args, rank, world, dev, name, torch.bfloat16,
                                                  1 << 28))
+                for pdt in (torch.bfloat16, torch.float32):
+                    try:
+                        zero1["runs"].append(run_sharded(args, rank, world, dev, name, pdt, None,
+                                                         param_gather="peer"))
+                    except (RuntimeError, ValueError) as e:   # no symmetric memory here
+                        torch.cuda.empty_cache()
+                        zero1["runs"].append({"model": name, "param_gather": "peer",
+                                              "unavailable": str(e)[:300]})
         zero1["nccl_reference"] = nccl_busbw(world, dev)
         if world > 1:
             zero1["zero1_parity"] = zero1_parity(world, rank, dev)

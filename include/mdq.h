@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define MDQ_ABI_VERSION 2
+#define MDQ_ABI_VERSION 3
 
 typedef enum mdq_status {
     MDQ_OK = 0,
@@ -114,6 +114,17 @@ typedef struct mdq_step_options {
                                           scale_reduce, quant, update_p) added by
                                           one thread per CTA; reference
                                           CUDA/stquant_kernel.cu:8-24,403-412     */
+    /* Peer copies (ABI version 3; no reference counterpart): the step also
+     * stores every updated parameter into n_peers other GPUs' memory, at the
+     * address of its local copy plus peer_delta[k] bytes.  The local copy is
+     * p_bf16 when a descriptor sets it (bf16 stores), else p (fp32 stores).
+     * For buffers mapped at the same layout on every GPU (symmetric memory),
+     * so that a sharded optimizer's step is also its parameter all-gather.
+     * 0..7 peers; block sizes that need the one-thread-per-element kernel
+     * (not a power of two, or below 8) are refused when n_peers > 0.        */
+    int32_t n_peers;
+    int32_t reserved;
+    int64_t peer_delta[7];
 } mdq_step_options;
 
 /*

@@ -219,8 +219,8 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
         for (int i = 0; i < 2; ++i) {
             const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
             if (FULL) {
-                __stcs(reinterpret_cast<float4*>(T.p + e),
-                       make_float4(p[4 * i + 0], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]));
+                const float4 pv = make_float4(p[4 * i + 0], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+                __stcs(reinterpret_cast<float4*>(T.p + e), pv);
                 if (T.p16 != nullptr) {
                     const __nv_bfloat162 lo = __floats2bfloat162_rn(p[4 * i + 0], p[4 * i + 1]);
                     const __nv_bfloat162 hi = __floats2bfloat162_rn(p[4 * i + 2], p[4 * i + 3]);
@@ -228,13 +228,22 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                     w.x = *reinterpret_cast<const unsigned*>(&lo);
                     w.y = *reinterpret_cast<const unsigned*>(&hi);
                     __stcs(reinterpret_cast<uint2*>(T.p16 + e), w);
+                    peer_store(X.peers, reinterpret_cast<uint2*>(T.p16 + e), w);
+                } else {
+                    peer_store(X.peers, reinterpret_cast<float4*>(T.p + e), pv);
                 }
             } else {
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     if (j < cnt[i]) {
                         T.p[e + j] = p[4 * i + j];
-                        if (T.p16 != nullptr) T.p16[e + j] = __float2bfloat16_rn(p[4 * i + j]);
+                        if (T.p16 != nullptr) {
+                            const __nv_bfloat16 b = __float2bfloat16_rn(p[4 * i + j]);
+                            T.p16[e + j] = b;
+                            peer_store(X.peers, T.p16 + e + j, b);
+                        } else {
+                            peer_store(X.peers, T.p + e + j, p[4 * i + j]);
+                        }
                     }
             }
         }
@@ -370,6 +379,7 @@ mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
             __syncwarp();
             if (lane == 0) {
                 const LaunchDesc& D = P.d[find_desc(P, u)];
+                X.peers = P.peers;
                 X.t = D.t;
                 X.n = D.n;
                 X.tile_begin = D.tile_begin;

@@ -45,6 +45,9 @@
 static_assert(offsetof(mdq_tensor_desc, grad_dtype) == 104, "mdq_tensor_desc layout");
 static_assert(offsetof(mdq_tensor_desc, p_bf16) == 112, "mdq_tensor_desc layout");
 static_assert(sizeof(mdq_tensor_desc) == 120, "mdq_tensor_desc layout");
+static_assert(offsetof(mdq_step_options, n_peers) == 16, "mdq_step_options layout");
+static_assert(offsetof(mdq_step_options, peer_delta) == 24, "mdq_step_options layout");
+static_assert(sizeof(mdq_step_options) == 80, "mdq_step_options layout");
 
 namespace mdq {
 
@@ -379,8 +382,10 @@ mdq_status launch_tree(const mdq_tensor_desc& d, bool exact, unsigned long long*
 // launches of at most CAP descriptors each.
 template <int CAP>
 mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bool exact,
-                     unsigned long long* prof, int sms, cudaStream_t s) {
+                     unsigned long long* prof, const mdq::PeerSet& peers, int sms,
+                     cudaStream_t s) {
     static thread_local mdq::LaunchParams<CAP> P;  // ~24 KB for CAP = 224
+    P.peers = peers;
     // 16 elements per thread (4096-element tiles, 2 CTAs per SM) halve the
     // per-tile work; measured on B200 it pays for 4-bit v codes, and for
     // 8-bit codes only with blocks of 1024 or more.
@@ -457,9 +462,25 @@ mdq_status mdq_adamw_step_multi(const mdq_tensor_desc* descs, int32_t n_descs,
     if (opts != nullptr && opts->p_mode != MDQ_P_FAST && opts->p_mode != MDQ_P_EXACT)
         return fail(MDQ_ERR_INVALID_ARG, "bad p_mode %d", opts->p_mode);
     unsigned long long* prof = opts ? opts->profile_cycles : nullptr;
+    mdq::PeerSet peers{};
+    if (opts != nullptr && opts->n_peers != 0) {
+        if (opts->n_peers < 0 || opts->n_peers > 7)
+            return fail(MDQ_ERR_INVALID_ARG, "n_peers %d outside 0..7", opts->n_peers);
+        peers.n = opts->n_peers;
+        for (int k = 0; k < peers.n; ++k) {
+            if (opts->peer_delta[k] == 0 || (opts->peer_delta[k] & 15) != 0)
+                return fail(MDQ_ERR_INVALID_ARG, "peer_delta[%d] must be a non-zero multiple of 16",
+                            k);
+            peers.delta[k] = opts->peer_delta[k];
+        }
+    }
     for (int i = 0; i < n_descs; ++i) {
         const mdq_status st = validate(descs[i], i);
         if (st != MDQ_OK) return st;
+        if (peers.n > 0 && descs[i].n > 0 && !fast_eligible(descs[i]))
+            return fail(MDQ_ERR_UNSUPPORTED,
+                        "desc %d: block %d needs the per-element kernel, which has no peer copies",
+                        i, descs[i].block);
     }
     int sms = 0;
     bool any_work = false;
@@ -488,8 +509,8 @@ mdq_status mdq_adamw_step_multi(const mdq_tensor_desc* descs, int32_t n_descs,
         if (cnt == 0) continue;
         const mdq_status st =
             cnt <= mdq::kCapSmall
-                ? run_class<mdq::kCapSmall>(descs, order, cnt, exact, prof, sms, stream)
-                : run_class<mdq::kCapLarge>(descs, order, cnt, exact, prof, sms, stream);
+                ? run_class<mdq::kCapSmall>(descs, order, cnt, exact, prof, peers, sms, stream)
+                : run_class<mdq::kCapLarge>(descs, order, cnt, exact, prof, peers, sms, stream);
         if (st != MDQ_OK) return st;
     }
     for (int i = 0; i < n_descs; ++i) {
@@ -549,7 +570,7 @@ mdq_status mdq_fused_adamw(float* p, const void* grad, int32_t grad_dtype, void*
     }
     if (d.layout != MDQ_LAYOUT_PACKED4 && (exp_avg_numel < n || exp_avg_sq_numel < n))
         return fail(MDQ_ERR_INVALID_ARG, "exp_avg / exp_avg_sq hold fewer elements than p");
-    mdq_step_options o;
+    mdq_step_options o = {};  // no peers
     o.p_mode = MDQ_P_EXACT;
     o.profile_cycles = profile_cycles;
     return mdq_adamw_step_multi(&d, 1, &o, stream);

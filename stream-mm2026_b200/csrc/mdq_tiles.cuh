@@ -60,16 +60,32 @@ struct LaunchDesc {
     int8_t m_bits, v_bits, log2_block, vec;
 };
 
+// Other GPUs that receive copies of the updated parameters (mdq_step_options).
+struct PeerSet {
+    int32_t n;
+    int64_t delta[7];
+};
+
 template <int CAP>
 struct LaunchParams {
     int32_t n_desc;
     int32_t total_tiles;
     unsigned long long* prof;
+    PeerSet peers;
     LaunchDesc d[CAP];
 };
 
+// Store `val` at the same position of every peer's copy of the buffer that
+// holds `local` (plain stores over NVLink into mapped peer memory).
+template <typename V>
+__device__ __forceinline__ void peer_store(const PeerSet& ps, V* local, const V& val) {
+    for (int k = 0; k < ps.n; ++k)
+        *reinterpret_cast<V*>(reinterpret_cast<char*>(local) + ps.delta[k]) = val;
+}
+
 // The tensor a CTA is working on, staged in shared memory by thread 0.
 struct TileCtx {
+    PeerSet peers;
     TensorPtrs t;
     int64_t n;
     int32_t tile_begin, tile_end;  // this tensor's tiles within the launch
@@ -306,7 +322,7 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     }
     if (T.p16 != nullptr) {
         // bf16 copy of the updated parameters (a sharded optimizer's
-        // all-gather send buffer), round to nearest even.
+        // all-gather send buffer), round to nearest even; and the peers' copies.
 #pragma unroll
         for (int i = 0; i < NCH; ++i) {
             const int64_t e = e_first + (int64_t)cstride * i;
@@ -317,10 +333,29 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                 w.x = *reinterpret_cast<const unsigned*>(&lo);
                 w.y = *reinterpret_cast<const unsigned*>(&hi);
                 __stcs(reinterpret_cast<uint2*>(T.p16 + e), w);
+                peer_store(X.peers, reinterpret_cast<uint2*>(T.p16 + e), w);
             } else {
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    if (j < cnt[i]) T.p16[e + j] = __float2bfloat16_rn(p[4 * i + j]);
+                    if (j < cnt[i]) {
+                        const __nv_bfloat16 b = __float2bfloat16_rn(p[4 * i + j]);
+                        T.p16[e + j] = b;
+                        peer_store(X.peers, T.p16 + e + j, b);
+                    }
+            }
+        }
+    } else if (X.peers.n > 0) {
+        // fp32 parameters: the peers' copies of the updated values.
+#pragma unroll
+        for (int i = 0; i < NCH; ++i) {
+            const int64_t e = e_first + (int64_t)cstride * i;
+            if (FULL) {
+                peer_store(X.peers, reinterpret_cast<float4*>(T.p + e),
+                           make_float4(p[4 * i + 0], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < cnt[i]) peer_store(X.peers, T.p + e + j, p[4 * i + j]);
             }
         }
     }
@@ -461,6 +496,7 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
             __syncthreads();  // every thread is done with the previous tensor
             if (tid == 0) {
                 const LaunchDesc& D = P.d[find_desc(P, tile)];
+                s_ctx.peers = P.peers;
                 s_ctx.t = D.t;
                 s_ctx.n = D.n;
                 s_ctx.tile_begin = D.tile_begin;

@@ -27,7 +27,7 @@ LAYOUT_PACKED4, LAYOUT_S8U8, LAYOUT_S16U16, LAYOUT_S32U32, LAYOUT_M8V4 = range(5
 # mdq_p_mode
 P_FAST, P_EXACT = 0, 1
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class TensorDesc(ctypes.Structure):
@@ -84,7 +84,9 @@ class FQDesc(ctypes.Structure):
 class StepOptions(ctypes.Structure):
     """Mirror of ``mdq_step_options``."""
 
-    _fields_ = [("p_mode", ctypes.c_int32), ("profile_cycles", ctypes.c_void_p)]
+    _fields_ = [("p_mode", ctypes.c_int32), ("profile_cycles", ctypes.c_void_p),
+                ("n_peers", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("peer_delta", ctypes.c_int64 * 7)]
 
 
 class MDQError(RuntimeError):

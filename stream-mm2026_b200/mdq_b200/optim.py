@@ -293,7 +293,8 @@ class MDQAdamWSimple(Optimizer):
             start = torch.cuda.Event(enable_timing=True)
             end = torch.cuda.Event(enable_timing=True)
             start.record()
-            kernels.run_descs(self._descs, len(items), device, self.p_mode, prof)
+            kernels.run_descs(self._descs, len(items), device, self.p_mode, prof,
+                              peer_deltas=getattr(self, "_peer_deltas", None))
             end.record()
         self._pending_events = (start, end, device)
 

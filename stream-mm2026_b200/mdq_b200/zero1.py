@@ -157,13 +157,20 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
     overlap the next forward; ``wait_param_gather()`` waits for all.
     ``profile_phases`` records CUDA events around the reduce-scatter, the
     step kernels and the all-gather; ``last_phase_ms()`` reads them.
+
+    ``param_gather="peer"`` (NCCL groups of up to 8 GPUs) puts the flat
+    parameter buffer in symmetric memory: the step kernel stores each updated
+    parameter into every rank's copy directly over NVLink (bf16 with bf16
+    parameters, else fp32), so the step is its own all-gather, and one small
+    all-reduce at the end orders the ranks.  "nccl" (default) all-gathers
+    each bucket with NCCL after its step kernel.
     """
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  alpha=0.9, layer_count=24, batch_size=32, update_freq=20, block_size=256,
                  *, process_group=None, grad_dtype=torch.float32, bucket_elems=None,
                  overlap_grad_reduce=False, param_dtype=torch.float32,
-                 overlap_param_gather=False, profile_phases=False, **kw):
+                 overlap_param_gather=False, profile_phases=False, param_gather="nccl", **kw):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                          alpha=alpha, layer_count=layer_count, batch_size=batch_size,
                          update_freq=update_freq, block_size=block_size, **kw)
@@ -202,7 +209,14 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
                 mo = self._master_off(pc)
                 src = self.params[pc.param].detach().reshape(-1)[pc.start:pc.start + pc.n]
                 self.master[mo:mo + pc.n].copy_(src)
-        self.flat_param = torch.zeros(self.layout.total, dtype=param_dtype, device=dev)
+        if param_gather not in ("nccl", "peer"):
+            raise ValueError("param_gather must be 'nccl' or 'peer'")
+        self.param_gather = param_gather
+        self._peer_deltas = None
+        if param_gather == "peer":
+            self.flat_param = self._symmetric_flat(param_dtype, dev)
+        else:
+            self.flat_param = torch.zeros(self.layout.total, dtype=param_dtype, device=dev)
         self.flat_grad = torch.zeros(self.layout.total, dtype=grad_dtype, device=dev)
         for p, off in zip(self.params, self.layout.offsets):
             n = p.numel()
@@ -278,6 +292,28 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             st["last_score"] = torch.tensor(12.0, device=p.device)
             st["piece"] = (pc.start, pc.n)
         return st
+
+    def _symmetric_flat(self, dtype, dev):
+        """The flat parameter buffer in symmetric memory (the same layout
+        mapped on every rank), for param_gather="peer": the step kernel then
+        stores each updated parameter into every rank's copy itself, over
+        NVLink, and the all-gather is a barrier."""
+        if not (dist.is_initialized() and dev.type == "cuda"
+                and dist.get_backend(self.group) == "nccl"):
+            raise RuntimeError("param_gather='peer' needs CUDA tensors and an NCCL process group")
+        if self.world > 8:
+            raise ValueError("param_gather='peer' supports up to 8 ranks")
+        import torch.distributed._symmetric_memory as symm_mem
+
+        flat = symm_mem.empty(self.layout.total, dtype=dtype, device=dev)
+        flat.zero_()
+        grp = self.group if self.group is not None else dist.group.WORLD
+        self._symm = symm_mem.rendezvous(flat, grp)
+        ptrs = list(self._symm.buffer_ptrs)
+        me = ptrs[self._symm.rank]
+        self._peer_deltas = [ptrs[r] - me for r in range(len(ptrs)) if r != self._symm.rank]
+        self._peer_token = torch.zeros(1, device=dev)
+        return flat
 
     def _master_off(self, pc: Piece) -> int:
         k = self._bucket_of_piece(pc)
@@ -516,7 +552,12 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             self._launch(items, device)
             for st, bits in repack:
                 self._pack_momentum_storage(st, bits)
-            self._all_gather_bucket(k)
+            if self.param_gather == "nccl":
+                self._all_gather_bucket(k)
+        if self.param_gather == "peer" and self.world > 1:
+            # The step kernels wrote every rank's copy; a collective on the
+            # stream orders every rank's kernels before anyone reads them.
+            dist.all_reduce(self._peer_token, group=self.group)
         if ev is not None:
             ev[2].record()
         if not self.overlap_param_gather:

@@ -78,6 +78,27 @@ def test_multi_rejects_bad_options():
     opts = StepOptions(7, None)
     assert lib.mdq_adamw_step_multi(arr, 1, ctypes.byref(opts), None) == MDQ_ERR_INVALID_ARG
     assert lib.mdq_adamw_step_multi(None, 2, None, None) == MDQ_ERR_INVALID_ARG
+    # Peer copies: at most 7 peers, deltas non-zero multiples of 16 bytes,
+    # and no peers for block sizes that need the per-element kernel.  All are
+    # refused before anything touches a device.
+    for n_peers, delta, msg in ((8, 16, "n_peers"), (1, 0, "peer_delta"), (1, 24, "peer_delta")):
+        opts = StepOptions(0, None)
+        opts.n_peers = n_peers
+        opts.peer_delta[0] = delta
+        assert lib.mdq_adamw_step_multi(arr, 1, ctypes.byref(opts), None) == MDQ_ERR_INVALID_ARG
+        assert msg in lib.mdq_last_error().decode()
+    opts = StepOptions(0, None)
+    opts.n_peers, opts.peer_delta[0] = 1, 1 << 30
+    odd = (TensorDesc * 1)(_desc(block=100))
+    assert lib.mdq_adamw_step_multi(odd, 1, ctypes.byref(opts), None) == MDQ_ERR_UNSUPPORTED
+    assert "no peer copies" in lib.mdq_last_error().decode()
+
+
+def test_step_options_layout():
+    import ctypes
+
+    assert ctypes.sizeof(StepOptions) == 80
+    assert StepOptions.n_peers.offset == 16 and StepOptions.peer_delta.offset == 24
 
 
 def test_empty_step_is_a_no_op():

@@ -30,7 +30,7 @@ def _params(device):
 KW = dict(lr=1e-3, weight_decay=0.01, block_size=256, p_mode="exact")
 
 
-def _worker(rank, world, port, steps, bits, overlap, q):
+def _worker(rank, world, port, steps, bits, overlap, q, gather="nccl"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
@@ -41,7 +41,7 @@ def _worker(rank, world, port, steps, bits, overlap, q):
         params = _params(torch.device("cuda", rank))
         extra = dict(bucket_elems=300_000, overlap_grad_reduce=True) if overlap else {}
         opt = ZeroMDQAdamW([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
-                           fixed_bits=bits, **KW, **extra)
+                           fixed_bits=bits, param_gather=gather, **KW, **extra)
         for t in range(1, steps + 1):
             opt.zero_grad()
             if overlap:
@@ -63,8 +63,12 @@ def _worker(rank, world, port, steps, bits, overlap, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("bits,overlap", [(4, False), ((8, 4), False), (8, False), ((8, 4), True)])
-def test_zero1_nccl_equals_unsharded(cuda_device, bits, overlap):
+@pytest.mark.parametrize("bits,overlap,gather", [(4, False, "nccl"), ((8, 4), False, "nccl"),
+                                                 (8, False, "nccl"), ((8, 4), True, "nccl"),
+                                                 ((8, 4), False, "peer"), (4, True, "peer")])
+def test_zero1_nccl_equals_unsharded(cuda_device, bits, overlap, gather):
+    """gather "peer": the step kernel itself stores the updated parameters
+    into every rank's copy (symmetric memory) instead of an NCCL all-gather."""
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs at least two GPUs")
@@ -84,7 +88,7 @@ def test_zero1_nccl_equals_unsharded(cuda_device, bits, overlap):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, bits, overlap, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, bits, overlap, q, gather))
              for r in range(world)]
     for p in procs:
         p.start()
