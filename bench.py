@@ -391,7 +391,8 @@ def _max_over_ranks(x, device, world):
     return t.tolist()
 
 
-def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems, param_gather="nccl"):
+def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems, param_gather="nccl",
+                grad_reduce="nccl"):
     """One ZeroMDQAdamW.step() of a fixed model on N GPUs (strong scaling:
     the model is the same at every N): bf16 gradients reduce-scattered over
     NCCL, the fused step on each rank's shard, parameters all-gathered.  The
@@ -411,7 +412,7 @@ def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems, para
     opt = ZeroMDQAdamW(params, lr=1e-3, weight_decay=0.01, block_size=spec["block"],
                        fixed_bits=spec["bits"], p_mode="fast", grad_dtype=torch.bfloat16,
                        param_dtype=param_dtype, bucket_elems=bucket_elems, profile_phases=True,
-                       param_gather=param_gather)
+                       param_gather=param_gather, grad_reduce=grad_reduce)
     del params
     opt.flat_grad.normal_(0, 1e-3, generator=torch.Generator(device=device).manual_seed(rank))
     for _ in range(3):
@@ -448,6 +449,8 @@ def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems, para
            "buckets": len(opt.layout.buckets), "steps": steps,
            "param_gather": ("step kernel stores into every rank's copy (symmetric memory, NVLink)"
                             if param_gather == "peer" else "NCCL all-gather per bucket"),
+           "grad_reduce": ("step kernel sums every rank's gradients (symmetric memory, NVLink)"
+                           if grad_reduce == "peer" else "NCCL reduce-scatter"),
            "ms_per_step": round(total_ms, 3),
            "gparams_per_s": round(n / (total_ms * 1e-3) / 1e9, 2),
            "phases_ms": {"reduce_scatter": round(rs_ms, 3), "step": round(step_ms, 3),
@@ -585,7 +588,9 @@ def zero1_parity(world, rank, device):
                             (dict(), torch.float32, "nccl"),
                             (dict(fixed_bits=4), torch.bfloat16, "nccl"),
                             (dict(fixed_bits=(8, 4)), torch.float32, "peer"),
-                            (dict(fixed_bits=4), torch.bfloat16, "peer")):
+                            (dict(fixed_bits=4), torch.bfloat16, "peer"),
+                            (dict(fixed_bits=(8, 4)), torch.float32, "peer+grad"),
+                            (dict(fixed_bits=4), torch.bfloat16, "peer+grad")):
         common = dict(lr=1e-3, weight_decay=0.01, block_size=256, p_mode="exact", **kw)
         ref = params()
         ref_opt = MDQAdamWSimpleFusedIO(ref, **common)
@@ -593,9 +598,11 @@ def zero1_parity(world, rank, device):
         try:
             opt = ZeroMDQAdamW(mine, bucket_elems=400_000, param_dtype=pdt,
                                grad_dtype=torch.bfloat16 if pdt == torch.bfloat16 else torch.float32,
-                               param_gather=gather, **common)
+                               param_gather=gather.split("+")[0],
+                               grad_reduce="peer" if gather.endswith("+grad") else "nccl",
+                               **common)
         except (RuntimeError, ValueError):
-            if gather == "peer":      # no symmetric memory on this box: nothing to check
+            if gather.startswith("peer"):   # no symmetric memory on this box: nothing to check
                 continue
             raise
         for t in range(1, 6):
@@ -836,10 +843,11 @@ def main() -> int:
             if world > 1:
                 zero1["runs"].append(run_sharded(args, rank, world, dev, name, torch.bfloat16,
                                                  1 << 28))
-                for pdt in (torch.bfloat16, torch.float32):
+                for pdt, gr in ((torch.bfloat16, "nccl"), (torch.float32, "nccl"),
+                                (torch.bfloat16, "peer")):
                     try:
                         zero1["runs"].append(run_sharded(args, rank, world, dev, name, pdt, None,
-                                                         param_gather="peer"))
+                                                         param_gather="peer", grad_reduce=gr))
                     except (RuntimeError, ValueError) as e:   # no symmetric memory here
                         torch.cuda.empty_cache()
                         zero1["runs"].append({"model": name, "param_gather": "peer",

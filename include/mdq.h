@@ -125,6 +125,17 @@ typedef struct mdq_step_options {
     int32_t n_peers;
     int32_t reserved;
     int64_t peer_delta[7];
+    /* Gradient reduction in the step (ABI version 3; no reference
+     * counterpart): with n_grad_ranks > 0 the gradient of an element is
+     * grad_scale * (sum over k < n_grad_ranks, in k order, of the value at
+     * the descriptor's grad address plus grad_delta[k] bytes), summed in fp32.
+     * With symmetric gradient buffers and one delta per rank in rank order
+     * (0 for the calling rank), this is the average over ranks that a
+     * reduce-scatter would have delivered to the shard's owner.  1..8 ranks;
+     * deltas multiples of 16.                                                */
+    int32_t n_grad_ranks;
+    float grad_scale;
+    int64_t grad_delta[8];
 } mdq_step_options;
 
 /*

@@ -84,7 +84,7 @@ template <typename GT> struct PreLoads {
 
 // One quantisation block (unit) of the tensor in X, starting at element e0.
 // FULL: all B elements in range and all pointers allow vector access.
-template <int LAYOUT, typename GT, bool EXACT_P, bool FULL, int LOGB, bool TBL>
+template <int LAYOUT, typename GT, bool EXACT_P, bool FULL, int LOGB, bool TBL, bool GR>
 __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* wm, float* wx,
                                            PreLoads<GT>& pre, int64_t next_e0) {
     using CI = Codes<LAYOUT>;
@@ -144,6 +144,12 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                 p[4 * i + 0] = pre.p[i].x; p[4 * i + 1] = pre.p[i].y;
                 p[4 * i + 2] = pre.p[i].z; p[4 * i + 3] = pre.p[i].w;
                 GradRaw<GT>::decode(pre.g[i], g + 4 * i);
+                if constexpr (GR) {   // gradients summed over ranks: load them now
+                    float gg[4];
+                    load_grad4<GT, GR>(T.g, e0 + 256 * s + 128 * i + 4 * lane, gg, X.granks);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) g[4 * i + j] = gg[j];
+                }
                 if constexpr (LAYOUT == MDQ_LAYOUT_PACKED4) {
                     raw[i].w = pre.m[i];   // the packed byte pairs, decoded by table
                 } else {
@@ -167,7 +173,7 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                     const float4 a = __ldcs(reinterpret_cast<const float4*>(T.p + e));
                     p[4 * i + 0] = a.x; p[4 * i + 1] = a.y; p[4 * i + 2] = a.z; p[4 * i + 3] = a.w;
                     float gg[4];
-                    Grad<GT>::load4(T.g, e, gg);
+                    load_grad4<GT, GR>(T.g, e, gg, X.granks);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) g[4 * i + j] = gg[j];
                     if constexpr (kTab) {
@@ -185,7 +191,7 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                         p[k] = 0.0f; g[k] = 0.0f; qm[k] = 0; qv[k] = 0;
                         if (j < cnt[i]) {
                             p[k] = T.p[e + j];
-                            g[k] = Grad<GT>::load1(T.g, e + j);
+                            g[k] = load_grad1<GT, GR>(T.g, e + j, X.granks);
                             CI::load1(T, e + j, qm[k], qv[k]);
                         }
                     }
@@ -346,18 +352,18 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
 
 // Partial or unaligned blocks (a tensor's tail) take an out-of-line copy of
 // the body, so the hot loop's code stays small.
-template <int LAYOUT, typename GT, bool EXACT_P, int LOGB, bool TBL>
+template <int LAYOUT, typename GT, bool EXACT_P, int LOGB, bool TBL, bool GR>
 __device__ __noinline__ void block_body_tail(const TileCtx& X, int64_t e0, float* wm, float* wx) {
     PreLoads<GT> none;
     none.valid = false;
-    block_body<LAYOUT, GT, EXACT_P, false, LOGB, TBL>(X, e0, wm, wx, none, -1);
+    block_body<LAYOUT, GT, EXACT_P, false, LOGB, TBL, GR>(X, e0, wm, wx, none, -1);
 }
 
 // Persistent grid: CTA c takes units [total c / grid, total (c+1) / grid),
 // warp w the units lo + w, lo + w + 8, ...; `tile_begin` of a descriptor
 // counts units (blocks) here.  Each warp stages the tensor it works on in its
 // own shared-memory slot.
-template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL>
+template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL, bool GR>
 __global__ void __launch_bounds__(kBlkThreads, blk_min_ctas<LOGB>())
 mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
     extern __shared__ __align__(16) float s_park[];
@@ -380,6 +386,7 @@ mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
             if (lane == 0) {
                 const LaunchDesc& D = P.d[find_desc(P, u)];
                 X.peers = P.peers;
+                X.granks = P.granks;
                 X.t = D.t;
                 X.n = D.n;
                 X.tile_begin = D.tile_begin;
@@ -398,17 +405,17 @@ mdq_step_blocks(const __grid_constant__ LaunchParams<CAP> P) {
             const int u2 = u + kBlkWarps;
             const int64_t e2 = (int64_t)(u2 - X.tile_begin) << LOGB;
             const int64_t next_e0 = (u2 < hi && u2 < cur_end && e2 + (1 << LOGB) <= X.n) ? e2 : -1;
-            block_body<LAYOUT, GT, EXACT_P, true, LOGB, TBL>(X, e0, wm, wx, pre, next_e0);
+            block_body<LAYOUT, GT, EXACT_P, true, LOGB, TBL, GR>(X, e0, wm, wx, pre, next_e0);
         } else {
             pre.valid = false;
-            block_body_tail<LAYOUT, GT, EXACT_P, LOGB, TBL>(X, e0, wm, wx);
+            block_body_tail<LAYOUT, GT, EXACT_P, LOGB, TBL, GR>(X, e0, wm, wx);
         }
     }
 }
 
-template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL>
+template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL, bool GR>
 mdq_status launch_blocks_t(const LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
-    auto k = mdq_step_blocks<LAYOUT, GT, EXACT_P, CAP, LOGB, TBL>;
+    auto k = mdq_step_blocks<LAYOUT, GT, EXACT_P, CAP, LOGB, TBL, GR>;
     constexpr int kSmem = blocks_smem_bytes<LOGB>();
     static int occ = 0;  // per instantiation; identical across B200 devices
     if (occ == 0) {
@@ -437,11 +444,18 @@ mdq_status launch_blocks_mode(const LaunchParams<CAP>& P, bool exact, int logb, 
                               cudaStream_t s) {
     constexpr bool kV4 = LAYOUT == MDQ_LAYOUT_PACKED4 || LAYOUT == MDQ_LAYOUT_M8V4;
     constexpr bool kT = kV4 && MDQ_USE_TABLES != 0;
+    if (P.granks.n > 0) {
+        if (logb == 10)
+            return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 10, kT, true>(P, sms, s)
+                         : launch_blocks_t<LAYOUT, GT, false, CAP, 10, kT, true>(P, sms, s);
+        return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 9, kT, true>(P, sms, s)
+                     : launch_blocks_t<LAYOUT, GT, false, CAP, 9, kT, true>(P, sms, s);
+    }
     if (logb == 10)
-        return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 10, kT>(P, sms, s)
-                     : launch_blocks_t<LAYOUT, GT, false, CAP, 10, kT>(P, sms, s);
-    return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 9, kT>(P, sms, s)
-                 : launch_blocks_t<LAYOUT, GT, false, CAP, 9, kT>(P, sms, s);
+        return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 10, kT, false>(P, sms, s)
+                     : launch_blocks_t<LAYOUT, GT, false, CAP, 10, kT, false>(P, sms, s);
+    return exact ? launch_blocks_t<LAYOUT, GT, true, CAP, 9, kT, false>(P, sms, s)
+                 : launch_blocks_t<LAYOUT, GT, false, CAP, 9, kT, false>(P, sms, s);
 }
 
 #define MDQ_BLOCKS_SIG(NAME, CAP)                                                               \

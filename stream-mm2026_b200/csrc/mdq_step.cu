@@ -47,7 +47,9 @@ static_assert(offsetof(mdq_tensor_desc, p_bf16) == 112, "mdq_tensor_desc layout"
 static_assert(sizeof(mdq_tensor_desc) == 120, "mdq_tensor_desc layout");
 static_assert(offsetof(mdq_step_options, n_peers) == 16, "mdq_step_options layout");
 static_assert(offsetof(mdq_step_options, peer_delta) == 24, "mdq_step_options layout");
-static_assert(sizeof(mdq_step_options) == 80, "mdq_step_options layout");
+static_assert(offsetof(mdq_step_options, n_grad_ranks) == 80, "mdq_step_options layout");
+static_assert(offsetof(mdq_step_options, grad_delta) == 88, "mdq_step_options layout");
+static_assert(sizeof(mdq_step_options) == 152, "mdq_step_options layout");
 
 namespace mdq {
 
@@ -382,10 +384,11 @@ mdq_status launch_tree(const mdq_tensor_desc& d, bool exact, unsigned long long*
 // launches of at most CAP descriptors each.
 template <int CAP>
 mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bool exact,
-                     unsigned long long* prof, const mdq::PeerSet& peers, int sms,
-                     cudaStream_t s) {
+                     unsigned long long* prof, const mdq::PeerSet& peers,
+                     const mdq::GradRanks& granks, int sms, cudaStream_t s) {
     static thread_local mdq::LaunchParams<CAP> P;  // ~24 KB for CAP = 224
     P.peers = peers;
+    P.granks = granks;
     // 16 elements per thread (4096-element tiles, 2 CTAs per SM) halve the
     // per-tile work; measured on B200 it pays for 4-bit v codes, and for
     // 8-bit codes only with blocks of 1024 or more.
@@ -474,9 +477,26 @@ mdq_status mdq_adamw_step_multi(const mdq_tensor_desc* descs, int32_t n_descs,
             peers.delta[k] = opts->peer_delta[k];
         }
     }
+    mdq::GradRanks granks{};
+    granks.scale = 1.0f;
+    if (opts != nullptr && opts->n_grad_ranks != 0) {
+        if (opts->n_grad_ranks < 0 || opts->n_grad_ranks > 8)
+            return fail(MDQ_ERR_INVALID_ARG, "n_grad_ranks %d outside 0..8", opts->n_grad_ranks);
+        granks.n = opts->n_grad_ranks;
+        granks.scale = opts->grad_scale;
+        for (int k = 0; k < granks.n; ++k) {
+            if ((opts->grad_delta[k] & 15) != 0)
+                return fail(MDQ_ERR_INVALID_ARG, "grad_delta[%d] must be a multiple of 16", k);
+            granks.delta[k] = opts->grad_delta[k];
+        }
+    }
     for (int i = 0; i < n_descs; ++i) {
         const mdq_status st = validate(descs[i], i);
         if (st != MDQ_OK) return st;
+        if (granks.n > 0 && descs[i].n > 0 && !fast_eligible(descs[i]))
+            return fail(MDQ_ERR_UNSUPPORTED,
+                        "desc %d: block %d needs the per-element kernel, which has no gradient "
+                        "reduction", i, descs[i].block);
         if (peers.n > 0 && descs[i].n > 0 && !fast_eligible(descs[i]))
             return fail(MDQ_ERR_UNSUPPORTED,
                         "desc %d: block %d needs the per-element kernel, which has no peer copies",
@@ -509,8 +529,10 @@ mdq_status mdq_adamw_step_multi(const mdq_tensor_desc* descs, int32_t n_descs,
         if (cnt == 0) continue;
         const mdq_status st =
             cnt <= mdq::kCapSmall
-                ? run_class<mdq::kCapSmall>(descs, order, cnt, exact, prof, peers, sms, stream)
-                : run_class<mdq::kCapLarge>(descs, order, cnt, exact, prof, peers, sms, stream);
+                ? run_class<mdq::kCapSmall>(descs, order, cnt, exact, prof, peers, granks, sms,
+                                            stream)
+                : run_class<mdq::kCapLarge>(descs, order, cnt, exact, prof, peers, granks, sms,
+                                            stream);
         if (st != MDQ_OK) return st;
     }
     for (int i = 0; i < n_descs; ++i) {

@@ -66,12 +66,20 @@ struct PeerSet {
     int64_t delta[7];
 };
 
+// Ranks whose gradient buffers are summed by the step (mdq_step_options).
+struct GradRanks {
+    int32_t n;
+    float scale;
+    int64_t delta[8];
+};
+
 template <int CAP>
 struct LaunchParams {
     int32_t n_desc;
     int32_t total_tiles;
     unsigned long long* prof;
     PeerSet peers;
+    GradRanks granks;
     LaunchDesc d[CAP];
 };
 
@@ -83,9 +91,44 @@ __device__ __forceinline__ void peer_store(const PeerSet& ps, V* local, const V&
         *reinterpret_cast<V*>(reinterpret_cast<char*>(local) + ps.delta[k]) = val;
 }
 
+// Four gradient values at element e: the local ones, or (GR: the launch has
+// gradient ranks) scale * the fp32 sum over the ranks' buffers in rank
+// order.  GR is a template parameter so that kernels without gradient ranks
+// keep their register allocation.
+template <typename GT, bool GR>
+__device__ __forceinline__ void load_grad4(const void* g, int64_t e, float (&o)[4],
+                                           const GradRanks& gr) {
+    if constexpr (!GR) {
+        Grad<GT>::load4(g, e, o);
+    } else {
+        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int k = 0; k < gr.n; ++k) {
+            float t[4];
+            Grad<GT>::load4(static_cast<const char*>(g) + gr.delta[k], e, t);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[j] = __fadd_rn(s[j], t[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = __fmul_rn(s[j], gr.scale);
+    }
+}
+
+template <typename GT, bool GR>
+__device__ __forceinline__ float load_grad1(const void* g, int64_t e, const GradRanks& gr) {
+    if constexpr (!GR) {
+        return Grad<GT>::load1(g, e);
+    } else {
+        float s = 0.0f;
+        for (int k = 0; k < gr.n; ++k)
+            s = __fadd_rn(s, Grad<GT>::load1(static_cast<const char*>(g) + gr.delta[k], e));
+        return __fmul_rn(s, gr.scale);
+    }
+}
+
 // The tensor a CTA is working on, staged in shared memory by thread 0.
 struct TileCtx {
     PeerSet peers;
+    GradRanks granks;
     TensorPtrs t;
     int64_t n;
     int32_t tile_begin, tile_end;  // this tensor's tiles within the launch
@@ -198,7 +241,7 @@ __device__ __forceinline__ QConsts make_q(float max_abs_m, float xmax, float xmi
 // 32*PT elements; a block of B > 32*PT elements spans B/(32*PT) warps.
 // FULL: every element in range and all pointers allow vector access.
 // `red` is this tile's cross-warp reduction scratch.
-template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL, int PT, bool TBL>
+template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL, int PT, bool TBL, bool GR>
 __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                                           float4* red,
                                           unsigned long long (&pc)[kProfSlots],
@@ -248,7 +291,7 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
             const float4 a = __ldcs(reinterpret_cast<const float4*>(T.p + e));
             p[4 * i + 0] = a.x; p[4 * i + 1] = a.y; p[4 * i + 2] = a.z; p[4 * i + 3] = a.w;
             float gg[4];
-            Grad<GT>::load4(T.g, e, gg);
+            load_grad4<GT, GR>(T.g, e, gg, X.granks);
 #pragma unroll
             for (int j = 0; j < 4; ++j) g[4 * i + j] = gg[j];
             if constexpr (kTab) {
@@ -266,7 +309,7 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                 p[k] = 0.0f; g[k] = 0.0f; qm[k] = 0; qv[k] = 0;
                 if (j < cnt[i]) {
                     p[k] = T.p[e + j];
-                    g[k] = Grad<GT>::load1(T.g, e + j);
+                    g[k] = load_grad1<GT, GR>(T.g, e + j, X.granks);
                     CI::load1(T, e + j, qm[k], qv[k]);
                 }
             }
@@ -475,7 +518,7 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
 // CTA-wide barriers happen only at a tensor switch and, for blocks spanning
 // several warps, inside the block reduction.
 // ---------------------------------------------------------------------------
-template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT, bool TBL>
+template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT, bool TBL, bool GR>
 __global__ void __launch_bounds__(threads_for<PT>(), PT == 8 ? MDQ_MIN_CTAS_PER_SM : MDQ_MIN_CTAS_PT16)
 mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
     constexpr int kTileT = kTile;
@@ -497,6 +540,7 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
             if (tid == 0) {
                 const LaunchDesc& D = P.d[find_desc(P, tile)];
                 s_ctx.peers = P.peers;
+                s_ctx.granks = P.granks;
                 s_ctx.t = D.t;
                 s_ctx.n = D.n;
                 s_ctx.tile_begin = D.tile_begin;
@@ -516,9 +560,9 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
 
         float4* red = s_red[tile & 1];
         if (s_ctx.vec && tile_e0 + kTileT <= n)
-            tile_body<LAYOUT, GT, EXACT_P, PROF, true, PT, TBL>(s_ctx, tile_e0, red, pc, t0);
+            tile_body<LAYOUT, GT, EXACT_P, PROF, true, PT, TBL, GR>(s_ctx, tile_e0, red, pc, t0);
         else
-            tile_body<LAYOUT, GT, EXACT_P, PROF, false, PT, TBL>(s_ctx, tile_e0, red, pc, t0);
+            tile_body<LAYOUT, GT, EXACT_P, PROF, false, PT, TBL, GR>(s_ctx, tile_e0, red, pc, t0);
     }
     if (PROF && tid == 0 && P.prof != nullptr) {
         for (int k = 0; k < kProfSlots; ++k) atomicAdd(P.prof + k, pc[k]);
@@ -539,9 +583,9 @@ int blocks_per_sm(K kernel, int threads) {
     return b;
 }
 
-template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT, bool TBL>
+template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT, bool TBL, bool GR>
 mdq_status launch_tiles_t(const LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
-    auto k = mdq_step_tiles<LAYOUT, GT, EXACT_P, PROF, CAP, PT, TBL>;
+    auto k = mdq_step_tiles<LAYOUT, GT, EXACT_P, PROF, CAP, PT, TBL, GR>;
     static int occ = 0;  // per instantiation; identical across B200 devices
     constexpr int kNT = threads_for<PT>();
     if (occ == 0) occ = blocks_per_sm(k, kNT);
@@ -556,12 +600,18 @@ mdq_status launch_tiles_t(const LaunchParams<CAP>& P, int sms, cudaStream_t stre
 template <int LAYOUT, typename GT, int CAP, int PT, bool TBL>
 mdq_status launch_tiles_pt(const LaunchParams<CAP>& P, bool exact, bool prof, int sms,
                            cudaStream_t s) {
-    if (exact) {
-        return prof ? launch_tiles_t<LAYOUT, GT, true, true, CAP, PT, TBL>(P, sms, s)
-                    : launch_tiles_t<LAYOUT, GT, true, false, CAP, PT, TBL>(P, sms, s);
+    // Launches that sum gradients over ranks take their own instantiation
+    // (without the clock64 profiler).
+    if (P.granks.n > 0) {
+        return exact ? launch_tiles_t<LAYOUT, GT, true, false, CAP, PT, TBL, true>(P, sms, s)
+                     : launch_tiles_t<LAYOUT, GT, false, false, CAP, PT, TBL, true>(P, sms, s);
     }
-    return prof ? launch_tiles_t<LAYOUT, GT, false, true, CAP, PT, TBL>(P, sms, s)
-                : launch_tiles_t<LAYOUT, GT, false, false, CAP, PT, TBL>(P, sms, s);
+    if (exact) {
+        return prof ? launch_tiles_t<LAYOUT, GT, true, true, CAP, PT, TBL, false>(P, sms, s)
+                    : launch_tiles_t<LAYOUT, GT, true, false, CAP, PT, TBL, false>(P, sms, s);
+    }
+    return prof ? launch_tiles_t<LAYOUT, GT, false, true, CAP, PT, TBL, false>(P, sms, s)
+                : launch_tiles_t<LAYOUT, GT, false, false, CAP, PT, TBL, false>(P, sms, s);
 }
 
 // Shapes instantiated per layout (chosen from B200 measurements): 4-bit-v

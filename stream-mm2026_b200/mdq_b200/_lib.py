@@ -86,7 +86,9 @@ class StepOptions(ctypes.Structure):
 
     _fields_ = [("p_mode", ctypes.c_int32), ("profile_cycles", ctypes.c_void_p),
                 ("n_peers", ctypes.c_int32), ("reserved", ctypes.c_int32),
-                ("peer_delta", ctypes.c_int64 * 7)]
+                ("peer_delta", ctypes.c_int64 * 7),
+                ("n_grad_ranks", ctypes.c_int32), ("grad_scale", ctypes.c_float),
+                ("grad_delta", ctypes.c_int64 * 8)]
 
 
 class MDQError(RuntimeError):

@@ -142,10 +142,14 @@ def fill_desc(d: TensorDesc, it: StepItem) -> None:
 
 def run_descs(descs, count: int, device: torch.device, p_mode: int = P_FAST,
               profile_cycles: Optional[torch.Tensor] = None, stream: Optional[int] = None,
-              peer_deltas: Optional[Sequence[int]] = None) -> None:
+              peer_deltas: Optional[Sequence[int]] = None,
+              grad_ranks: Optional[tuple] = None) -> None:
     """Launch a prepared ``TensorDesc`` array (the optimizer keeps one alive).
     ``peer_deltas``: byte offsets from each updated parameter's local copy
-    (p_bf16, else p) to its copies on other GPUs (mdq_step_options)."""
+    (p_bf16, else p) to its copies on other GPUs.  ``grad_ranks``: (scale,
+    byte offsets of every rank's gradient buffer in rank order, 0 for this
+    rank): the step sums the ranks' gradients and scales the sum
+    (mdq_step_options)."""
     opts = StepOptions(p_mode, profile_cycles.data_ptr() if profile_cycles is not None else None)
     if peer_deltas:
         if len(peer_deltas) > 7:
@@ -153,6 +157,14 @@ def run_descs(descs, count: int, device: torch.device, p_mode: int = P_FAST,
         opts.n_peers = len(peer_deltas)
         for k, dlt in enumerate(peer_deltas):
             opts.peer_delta[k] = int(dlt)
+    if grad_ranks:
+        scale, deltas = grad_ranks
+        if len(deltas) > 8:
+            raise ValueError("at most 8 gradient ranks")
+        opts.n_grad_ranks = len(deltas)
+        opts.grad_scale = float(scale)
+        for k, dlt in enumerate(deltas):
+            opts.grad_delta[k] = int(dlt)
     lib = _lib.load()
     with torch.cuda.device(device):
         st = lib.mdq_adamw_step_multi(descs, count, ctypes.byref(opts),

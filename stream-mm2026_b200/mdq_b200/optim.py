@@ -294,7 +294,8 @@ class MDQAdamWSimple(Optimizer):
             end = torch.cuda.Event(enable_timing=True)
             start.record()
             kernels.run_descs(self._descs, len(items), device, self.p_mode, prof,
-                              peer_deltas=getattr(self, "_peer_deltas", None))
+                              peer_deltas=getattr(self, "_peer_deltas", None),
+                              grad_ranks=getattr(self, "_grad_ranks", None))
             end.record()
         self._pending_events = (start, end, device)
 

@@ -163,14 +163,19 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
     parameter into every rank's copy directly over NVLink (bf16 with bf16
     parameters, else fp32), so the step is its own all-gather, and one small
     all-reduce at the end orders the ranks.  "nccl" (default) all-gathers
-    each bucket with NCCL after its step kernel.
+    each bucket with NCCL after its step kernel.  ``grad_reduce="peer"``
+    (with ``fixed_bits``) puts the gradients in symmetric memory too: instead
+    of a reduce-scatter, the step kernel reads every rank's gradient of each
+    element it owns over NVLink and averages them (fp32 sum in rank order),
+    so one kernel does reduce-scatter, step and all-gather.
     """
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  alpha=0.9, layer_count=24, batch_size=32, update_freq=20, block_size=256,
                  *, process_group=None, grad_dtype=torch.float32, bucket_elems=None,
                  overlap_grad_reduce=False, param_dtype=torch.float32,
-                 overlap_param_gather=False, profile_phases=False, param_gather="nccl", **kw):
+                 overlap_param_gather=False, profile_phases=False, param_gather="nccl",
+                 grad_reduce="nccl", **kw):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                          alpha=alpha, layer_count=layer_count, batch_size=batch_size,
                          update_freq=update_freq, block_size=block_size, **kw)
@@ -213,11 +218,24 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
             raise ValueError("param_gather must be 'nccl' or 'peer'")
         self.param_gather = param_gather
         self._peer_deltas = None
+        if grad_reduce not in ("nccl", "peer"):
+            raise ValueError("grad_reduce must be 'nccl' or 'peer'")
+        self.grad_reduce = grad_reduce
+        self._grad_ranks = None
         if param_gather == "peer":
-            self.flat_param = self._symmetric_flat(param_dtype, dev)
+            self.flat_param, deltas = self._symmetric_flat(param_dtype, dev)
+            self._peer_deltas = [d for r, d in enumerate(deltas) if r != self.rank]
         else:
             self.flat_param = torch.zeros(self.layout.total, dtype=param_dtype, device=dev)
-        self.flat_grad = torch.zeros(self.layout.total, dtype=grad_dtype, device=dev)
+        if grad_reduce == "peer":
+            if self.fixed_bits is None:
+                raise ValueError("grad_reduce='peer' needs fixed_bits: the bit policy reads the "
+                                 "reduced gradients before the step")
+            self.flat_grad, deltas = self._symmetric_flat(grad_dtype, dev)
+            self._grad_ranks = (1.0 / self.world, deltas)
+            overlap_grad_reduce = False
+        else:
+            self.flat_grad = torch.zeros(self.layout.total, dtype=grad_dtype, device=dev)
         for p, off in zip(self.params, self.layout.offsets):
             n = p.numel()
             self.flat_param[off:off + n].copy_(p.detach().reshape(-1))
@@ -294,26 +312,28 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         return st
 
     def _symmetric_flat(self, dtype, dev):
-        """The flat parameter buffer in symmetric memory (the same layout
-        mapped on every rank), for param_gather="peer": the step kernel then
-        stores each updated parameter into every rank's copy itself, over
-        NVLink, and the all-gather is a barrier."""
+        """A flat buffer in symmetric memory (the same layout mapped on every
+        rank) and the byte offsets from it to every rank's copy, in rank
+        order (0 for this rank).  param_gather="peer": the step kernel stores
+        each updated parameter into every rank's copy of the parameters;
+        grad_reduce="peer": it sums every rank's copy of the gradients."""
         if not (dist.is_initialized() and dev.type == "cuda"
                 and dist.get_backend(self.group) == "nccl"):
-            raise RuntimeError("param_gather='peer' needs CUDA tensors and an NCCL process group")
+            raise RuntimeError("peer gathers and reductions need CUDA tensors and an NCCL "
+                               "process group")
         if self.world > 8:
-            raise ValueError("param_gather='peer' supports up to 8 ranks")
+            raise ValueError("peer gathers and reductions support up to 8 ranks")
         import torch.distributed._symmetric_memory as symm_mem
 
         flat = symm_mem.empty(self.layout.total, dtype=dtype, device=dev)
         flat.zero_()
         grp = self.group if self.group is not None else dist.group.WORLD
-        self._symm = symm_mem.rendezvous(flat, grp)
-        ptrs = list(self._symm.buffer_ptrs)
-        me = ptrs[self._symm.rank]
-        self._peer_deltas = [ptrs[r] - me for r in range(len(ptrs)) if r != self._symm.rank]
+        handle = symm_mem.rendezvous(flat, grp)
+        self._symm_handles = getattr(self, "_symm_handles", []) + [handle]
+        ptrs = list(handle.buffer_ptrs)
+        me = ptrs[handle.rank]
         self._peer_token = torch.zeros(1, device=dev)
-        return flat
+        return flat, [ptr - me for ptr in ptrs]
 
     def _master_off(self, pc: Piece) -> int:
         k = self._bucket_of_piece(pc)
@@ -500,7 +520,13 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
         # A pending all-gather of the previous step must land before the
         # parameters are touched again.
         self.wait_param_gather()
-        self._reduce_scatter_grads()
+        if self.grad_reduce == "peer":
+            # Every rank's gradients are complete before any step kernel
+            # reads them (the kernels sum the ranks' copies themselves).
+            if self.world > 1:
+                dist.all_reduce(self._peer_token, group=self.group)
+        else:
+            self._reduce_scatter_grads()
         if ev is not None:
             ev[1].record()
         for pc in self.pieces:
@@ -554,9 +580,11 @@ class ZeroMDQAdamW(MDQAdamWSimpleFusedIO):
                 self._pack_momentum_storage(st, bits)
             if self.param_gather == "nccl":
                 self._all_gather_bucket(k)
-        if self.param_gather == "peer" and self.world > 1:
-            # The step kernels wrote every rank's copy; a collective on the
-            # stream orders every rank's kernels before anyone reads them.
+        if (self.param_gather == "peer" or self.grad_reduce == "peer") and self.world > 1:
+            # The step kernels wrote every rank's copy of the parameters or
+            # read every rank's gradients: a collective on the stream orders
+            # every rank's kernels before the parameters are read or the
+            # gradients overwritten.
             dist.all_reduce(self._peer_token, group=self.group)
         if ev is not None:
             ev[2].record()

@@ -87,6 +87,12 @@ def test_multi_rejects_bad_options():
         opts.peer_delta[0] = delta
         assert lib.mdq_adamw_step_multi(arr, 1, ctypes.byref(opts), None) == MDQ_ERR_INVALID_ARG
         assert msg in lib.mdq_last_error().decode()
+    for n, delta, msg in ((9, 0, "n_grad_ranks"), (2, 8, "grad_delta")):
+        opts = StepOptions(0, None)
+        opts.n_grad_ranks, opts.grad_scale = n, 0.5
+        opts.grad_delta[1] = delta
+        assert lib.mdq_adamw_step_multi(arr, 1, ctypes.byref(opts), None) == MDQ_ERR_INVALID_ARG
+        assert msg in lib.mdq_last_error().decode()
     opts = StepOptions(0, None)
     opts.n_peers, opts.peer_delta[0] = 1, 1 << 30
     odd = (TensorDesc * 1)(_desc(block=100))
@@ -97,8 +103,9 @@ def test_multi_rejects_bad_options():
 def test_step_options_layout():
     import ctypes
 
-    assert ctypes.sizeof(StepOptions) == 80
+    assert ctypes.sizeof(StepOptions) == 152
     assert StepOptions.n_peers.offset == 16 and StepOptions.peer_delta.offset == 24
+    assert StepOptions.n_grad_ranks.offset == 80 and StepOptions.grad_delta.offset == 88
 
 
 def test_empty_step_is_a_no_op():

@@ -41,7 +41,9 @@ def _worker(rank, world, port, steps, bits, overlap, q, gather="nccl"):
         params = _params(torch.device("cuda", rank))
         extra = dict(bucket_elems=300_000, overlap_grad_reduce=True) if overlap else {}
         opt = ZeroMDQAdamW([{"params": params[:4]}, {"params": params[4:], "weight_decay": 0.0}],
-                           fixed_bits=bits, param_gather=gather, **KW, **extra)
+                           fixed_bits=bits, param_gather=gather.split("+")[0],
+                           grad_reduce="peer" if gather.endswith("+grad") else "nccl",
+                           **KW, **extra)
         for t in range(1, steps + 1):
             opt.zero_grad()
             if overlap:
@@ -65,10 +67,13 @@ def _worker(rank, world, port, steps, bits, overlap, q, gather="nccl"):
 
 @pytest.mark.parametrize("bits,overlap,gather", [(4, False, "nccl"), ((8, 4), False, "nccl"),
                                                  (8, False, "nccl"), ((8, 4), True, "nccl"),
-                                                 ((8, 4), False, "peer"), (4, True, "peer")])
+                                                 ((8, 4), False, "peer"), (4, True, "peer"),
+                                                 ((8, 4), False, "peer+grad"), (8, False, "peer+grad")])
 def test_zero1_nccl_equals_unsharded(cuda_device, bits, overlap, gather):
     """gather "peer": the step kernel itself stores the updated parameters
-    into every rank's copy (symmetric memory) instead of an NCCL all-gather."""
+    into every rank's copy (symmetric memory) instead of an NCCL all-gather;
+    "peer+grad": it also sums every rank's gradients instead of an NCCL
+    reduce-scatter."""
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs at least two GPUs")
