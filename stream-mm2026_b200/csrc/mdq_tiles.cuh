@@ -125,6 +125,27 @@ __device__ __forceinline__ float load_grad1(const void* g, int64_t e, const Grad
     }
 }
 
+// Remote gradients staged ahead (gradient ranks, bf16 gradients, PT = 16):
+// each thread copies its own elements of the next tile from up to kStagedPeers
+// other ranks into its own shared-memory slots with cp.async (plain 8-byte
+// global-to-shared copies from mapped peer memory; the hardware's
+// wait_group, no polling), so the NVLink latency of tile t+1 overlaps the
+// math of tile t.  With more ranks, or other shapes, gradients are loaded
+// directly.
+constexpr int kStagedPeers = 3;
+constexpr int kStageDepth = 2;   // tiles staged ahead
+constexpr int kStageThreads = 128;
+constexpr int kStageChunks = 4;
+
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+    const unsigned a = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(a), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // The tensor a CTA is working on, staged in shared memory by thread 0.
 struct TileCtx {
     PeerSet peers;
@@ -245,7 +266,8 @@ template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, bool FULL, int PT, b
 __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                                           float4* red,
                                           unsigned long long (&pc)[kProfSlots],
-                                          unsigned long long& t0) {
+                                          unsigned long long& t0,
+                                          const uint2* stg = nullptr) {
     using CI = Codes<LAYOUT>;
     using TC = TableCodes<LAYOUT>;
     constexpr int NCH = PT / 4;
@@ -291,7 +313,34 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
             const float4 a = __ldcs(reinterpret_cast<const float4*>(T.p + e));
             p[4 * i + 0] = a.x; p[4 * i + 1] = a.y; p[4 * i + 2] = a.z; p[4 * i + 3] = a.w;
             float gg[4];
-            load_grad4<GT, GR>(T.g, e, gg, X.granks);
+            if constexpr (GR && sizeof(GT) == 2 && PT == 16) {
+                if (stg != nullptr) {
+                    // This rank's values from memory, the others' from the
+                    // staged copies; summed in rank order.
+                    float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    int slot = 0;
+                    for (int k = 0; k < X.granks.n; ++k) {
+                        uint2 w;
+                        if (X.granks.delta[k] == 0) {
+                            w = __ldcs(reinterpret_cast<const uint2*>(
+                                static_cast<const __nv_bfloat16*>(T.g) + e));
+                        } else {
+                            w = stg[(slot * kStageChunks + i) * kStageThreads + threadIdx.x];
+                            ++slot;
+                        }
+                        sacc[0] = __fadd_rn(sacc[0], __uint_as_float(w.x << 16));
+                        sacc[1] = __fadd_rn(sacc[1], __uint_as_float(w.x & 0xffff0000u));
+                        sacc[2] = __fadd_rn(sacc[2], __uint_as_float(w.y << 16));
+                        sacc[3] = __fadd_rn(sacc[3], __uint_as_float(w.y & 0xffff0000u));
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) gg[j] = __fmul_rn(sacc[j], X.granks.scale);
+                } else {
+                    load_grad4<GT, GR>(T.g, e, gg, X.granks);
+                }
+            } else {
+                load_grad4<GT, GR>(T.g, e, gg, X.granks);
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) g[4 * i + j] = gg[j];
             if constexpr (kTab) {
@@ -533,6 +582,10 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
     const int tile_lo = (int)(total * blockIdx.x / gridDim.x);
     const int tile_hi = (int)(total * (blockIdx.x + 1) / gridDim.x);
     int cur_end = -1;
+    constexpr bool kStage = GR && sizeof(GT) == 2 && PT == 16;
+    __shared__ uint2 s_stage[kStage ? kStageDepth + 1 : 1][kStage ? kStagedPeers : 1]
+                            [kStage ? kStageChunks : 1][kStage ? kStageThreads : 1];
+    int next_issue = tile_lo;   // first tile whose copies are not issued yet
 
     for (int tile = tile_lo; tile < tile_hi; ++tile) {
         if (tile >= cur_end) {
@@ -559,8 +612,50 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
         const int64_t tile_e0 = (int64_t)(tile - s_ctx.tile_begin) << kLogTileT;
 
         float4* red = s_red[tile & 1];
-        if (s_ctx.vec && tile_e0 + kTileT <= n)
-            tile_body<LAYOUT, GT, EXACT_P, PROF, true, PT, TBL, GR>(s_ctx, tile_e0, red, pc, t0);
+        const bool full = s_ctx.vec && tile_e0 + kTileT <= n;
+        const uint2* stg = nullptr;
+        if constexpr (kStage) {
+            const int np = s_ctx.granks.n - 1;       // other ranks
+            if (np >= 1 && np <= kStagedPeers) {
+                if (tile >= next_issue) next_issue = tile;   // (a new run of tiles)
+                // Keep the copies of up to kStageDepth tiles ahead in flight,
+                // one commit group per tile, within this tensor's full tiles.
+                const int lgL = min(5, s_ctx.lb - 4);
+                const int L = 1 << lgL;
+                const int lane = tid & 31, w = tid >> 5;
+                const int64_t within = (int64_t)w * 512 + ((lane >> lgL) << (lgL + 4)) +
+                                       4 * (lane & (L - 1));
+                while (next_issue <= tile + kStageDepth && next_issue < tile_hi &&
+                       next_issue < cur_end) {
+                    const int64_t e_t = (int64_t)(next_issue - s_ctx.tile_begin) << kLogTileT;
+                    if (!(s_ctx.vec && e_t + kTileT <= n)) break;   // tail tile: loaded directly
+                    const int slot_stage = next_issue % (kStageDepth + 1);
+                    int slot = 0;
+                    for (int k = 0; k < s_ctx.granks.n; ++k) {
+                        if (s_ctx.granks.delta[k] == 0) continue;
+                        const char* base = static_cast<const char*>(s_ctx.t.g) + s_ctx.granks.delta[k];
+#pragma unroll
+                        for (int i = 0; i < kStageChunks; ++i) {
+                            const int64_t e = e_t + within + (int64_t)(4 * L) * i;
+                            cp_async8(&s_stage[slot_stage][slot][i][tid], base + 2 * e);
+                        }
+                        ++slot;
+                    }
+                    cp_async_commit();
+                    ++next_issue;
+                }
+                if (tile < next_issue) {
+                    // Groups committed after this tile's own may stay in flight.
+                    const int after = next_issue - 1 - tile;
+                    if (after >= 2) cp_async_wait<2>();
+                    else if (after == 1) cp_async_wait<1>();
+                    else cp_async_wait<0>();
+                    if (full) stg = &s_stage[tile % (kStageDepth + 1)][0][0][0];
+                }
+            }
+        }
+        if (full)
+            tile_body<LAYOUT, GT, EXACT_P, PROF, true, PT, TBL, GR>(s_ctx, tile_e0, red, pc, t0, stg);
         else
             tile_body<LAYOUT, GT, EXACT_P, PROF, false, PT, TBL, GR>(s_ctx, tile_e0, red, pc, t0);
     }
