@@ -417,11 +417,15 @@ template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB, bool TBL, bo
 mdq_status launch_blocks_t(const LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
     auto k = mdq_step_blocks<LAYOUT, GT, EXACT_P, CAP, LOGB, TBL, GR>;
     constexpr int kSmem = blocks_smem_bytes<LOGB>();
-    static int occ = 0;  // per instantiation; identical across B200 devices
-    if (occ == 0) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    // The shared-memory attribute is per device: set on every launch.
+    {
+        const cudaError_t e =
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess)
             return mdq_fail(MDQ_ERR_CUDA, "block kernel smem attribute: %s", cudaGetErrorString(e));
+    }
+    static int occ = 0;  // per instantiation; identical across B200 devices
+    if (occ == 0) {
         int b = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, kBlkThreads, kSmem) != cudaSuccess ||
             b < 1)

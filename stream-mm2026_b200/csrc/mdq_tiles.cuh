@@ -126,13 +126,12 @@ __device__ __forceinline__ float load_grad1(const void* g, int64_t e, const Grad
 }
 
 // Remote gradients staged ahead (gradient ranks, bf16 gradients, PT = 16):
-// each thread copies its own elements of the next tile from up to kStagedPeers
-// other ranks into its own shared-memory slots with cp.async (plain 8-byte
-// global-to-shared copies from mapped peer memory; the hardware's
-// wait_group, no polling), so the NVLink latency of tile t+1 overlaps the
-// math of tile t.  With more ranks, or other shapes, gradients are loaded
-// directly.
-constexpr int kStagedPeers = 3;
+// each thread copies its own elements of the next kStageDepth tiles from the
+// other ranks (up to 7) into its own shared-memory slots with cp.async (plain
+// 8-byte global-to-shared copies from mapped peer memory; the hardware's
+// wait_group, no polling), so the NVLink latency of a tile overlaps the math
+// of the tiles before it.  Other shapes load the peers' gradients directly.
+constexpr int kStagedPeers = 7;
 constexpr int kStageDepth = 2;   // tiles staged ahead
 constexpr int kStageThreads = 128;
 constexpr int kStageChunks = 4;
@@ -583,8 +582,10 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
     const int tile_hi = (int)(total * (blockIdx.x + 1) / gridDim.x);
     int cur_end = -1;
     constexpr bool kStage = GR && sizeof(GT) == 2 && PT == 16;
-    __shared__ uint2 s_stage[kStage ? kStageDepth + 1 : 1][kStage ? kStagedPeers : 1]
-                            [kStage ? kStageChunks : 1][kStage ? kStageThreads : 1];
+    // Staging slots (dynamic shared memory, sized by the launch for the
+    // number of other ranks): [stage][rank slot][chunk][thread].
+    extern __shared__ __align__(16) uint2 s_stage[];
+    const int n_other = P.granks.n - 1;
     int next_issue = tile_lo;   // first tile whose copies are not issued yet
 
     for (int tile = tile_lo; tile < tile_hi; ++tile) {
@@ -637,7 +638,9 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
 #pragma unroll
                         for (int i = 0; i < kStageChunks; ++i) {
                             const int64_t e = e_t + within + (int64_t)(4 * L) * i;
-                            cp_async8(&s_stage[slot_stage][slot][i][tid], base + 2 * e);
+                            cp_async8(&s_stage[((slot_stage * n_other + slot) * kStageChunks + i) *
+                                               kStageThreads + tid],
+                                      base + 2 * e);
                         }
                         ++slot;
                     }
@@ -650,7 +653,9 @@ mdq_step_tiles(const __grid_constant__ LaunchParams<CAP> P) {
                     if (after >= 2) cp_async_wait<2>();
                     else if (after == 1) cp_async_wait<1>();
                     else cp_async_wait<0>();
-                    if (full) stg = &s_stage[tile % (kStageDepth + 1)][0][0][0];
+                    if (full)
+                        stg = &s_stage[(tile % (kStageDepth + 1)) * n_other * kStageChunks *
+                                       kStageThreads];
                 }
             }
         }
@@ -681,12 +686,33 @@ int blocks_per_sm(K kernel, int threads) {
 template <int LAYOUT, typename GT, bool EXACT_P, bool PROF, int CAP, int PT, bool TBL, bool GR>
 mdq_status launch_tiles_t(const LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
     auto k = mdq_step_tiles<LAYOUT, GT, EXACT_P, PROF, CAP, PT, TBL, GR>;
-    static int occ = 0;  // per instantiation; identical across B200 devices
     constexpr int kNT = threads_for<PT>();
-    if (occ == 0) occ = blocks_per_sm(k, kNT);
+    constexpr bool kStage = GR && sizeof(GT) == 2 && PT == 16;
+    int occ = 0;
+    size_t smem = 0;
+    if constexpr (kStage) {
+        // Staging slots for the other ranks' gradients (up to 7 x 3 x 4 KB).
+        const int n_other = P.granks.n - 1;
+        if (n_other >= 1 && n_other <= kStagedPeers)
+            smem = (size_t)(kStageDepth + 1) * n_other * kStageChunks * kStageThreads *
+                   sizeof(uint2);
+        // (set on every launch: the attribute is per device)
+        const cudaError_t ea = cudaFuncSetAttribute(
+            k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            (int)((kStageDepth + 1) * kStagedPeers * kStageChunks * kStageThreads * sizeof(uint2)));
+        if (ea != cudaSuccess)
+            return mdq_fail(MDQ_ERR_CUDA, "staging smem attribute: %s", cudaGetErrorString(ea));
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kNT, smem) != cudaSuccess ||
+            occ < 1)
+            occ = 1;
+    } else {
+        static int occ_s = 0;  // per instantiation; identical across B200 devices
+        if (occ_s == 0) occ_s = blocks_per_sm(k, kNT);
+        occ = occ_s;
+    }
     int grid = sms * occ;
     if (grid > P.total_tiles) grid = P.total_tiles;
-    k<<<grid, kNT, 0, stream>>>(P);
+    k<<<grid, kNT, smem, stream>>>(P);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return mdq_fail(MDQ_ERR_CUDA, "step launch: %s", cudaGetErrorString(e));
     return MDQ_OK;
