@@ -457,11 +457,17 @@ def run_sharded(args, rank, world, device, name, param_dtype, bucket_elems, para
                          "all_gather_tail": round(ag_ms, 3)},
            "step_only_gparams_per_s": round(n / (step_ms * 1e-3) / 1e9, 2)}
     if world > 1:
+        # Bus bandwidths only for phases that are a separate NCCL collective.
         out["nvlink"] = {
             "rs_bytes_per_gpu": rs_bytes, "ag_bytes_per_gpu": ag_bytes,
-            "rs_busbw_gbs": round(rs_bytes / (rs_ms * 1e-3) / 1e9, 1) if rs_ms > 0 else None,
+            "rs_busbw_gbs": (round(rs_bytes / (rs_ms * 1e-3) / 1e9, 1)
+                             if grad_reduce == "nccl" and rs_ms > 0 else None),
             "ag_busbw_gbs": (round(ag_bytes / (ag_ms * 1e-3) / 1e9, 1)
-                             if len(opt.layout.buckets) == 1 and ag_ms > 0 else None)}
+                             if param_gather == "nccl" and len(opt.layout.buckets) == 1
+                             and ag_ms > 0 else None)}
+        if param_gather == "peer":
+            # The step kernel carries the gather: bytes leaving each GPU per ms of step.
+            out["nvlink"]["step_out_gbs"] = round(ag_bytes / (step_ms * 1e-3) / 1e9, 1)
     del opt
     torch.cuda.empty_cache()
     return out
