@@ -82,6 +82,88 @@ template <typename GT> struct PreLoads {
     }
 };
 
+// Where pass 1 parks a lane's m and x = v + 1e-12 for pass 2: elements
+// 256 s + 128 i + 4 lane + (0..3) of the block, as one float4 each.
+struct ParkSplit {
+    float* wm;
+    float* wx;
+    __device__ float* m(int s, int i, int lane) const { return wm + 256 * s + 128 * i + 4 * lane; }
+    __device__ float* x(int s, int i, int lane) const { return wx + 256 * s + 128 * i + 4 * lane; }
+};
+
+// Pass 2 of a block (CUDA/stquant_kernel.cu:204-216): requantises the parked
+// m and x of the block at e0 with the block's new constants Q and stores the
+// codes.  Each lane reads back only what it parked itself.
+template <int LAYOUT, bool FULL, int LOGB, typename PARK>
+__device__ __forceinline__ void requant_block(const TileCtx& X, int64_t e0, const QConsts& Q,
+                                              const PARK& park) {
+    using CI = Codes<LAYOUT>;
+    constexpr int S = (1 << LOGB) / 256;
+    constexpr bool kApprox = CI::kApproxLog;
+    constexpr bool kMagicC = CI::kMagicCodes;
+    constexpr int kB = CI::kMBias;
+    const int lane = threadIdx.x & 31;
+    const TensorPtrs T = X.t;
+    const StepConsts& C = X.C;
+    const int64_t n = X.n;
+    constexpr bool kCorrect = !kApprox;
+#pragma unroll 1
+    for (int s = 0; s < S; ++s) {
+        float m[8], x[8];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float4 a = *reinterpret_cast<const float4*>(park.m(s, i, lane));
+            const float4 b = *reinterpret_cast<const float4*>(park.x(s, i, lane));
+            m[4 * i + 0] = a.x; m[4 * i + 1] = a.y; m[4 * i + 2] = a.z; m[4 * i + 3] = a.w;
+            x[4 * i + 0] = b.x; x[4 * i + 1] = b.y; x[4 * i + 2] = b.z; x[4 * i + 3] = b.w;
+        }
+        int mw[8], vw[8];
+        float rem_m = 0.0f, rem_v = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float rr;
+            mw[k] = min(round_checked<kCorrect, kB>(__fmul_rn(m[k], Q.rdm), m[k], Q.dm,
+                                                    Q.half_dm, rr), Q.mw_hi);
+            rem_m = max_nan(rem_m, rr);
+            const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -Q.lmin)
+                                     : __fsub_rn(logf(x[k]), Q.lmin);
+            vw[k] = round_checked<kCorrect>(__fmul_rn(xv, Q.rdv), xv, Q.dv, Q.half_dv, rr);
+            rem_v = max_nan(rem_v, rr);
+        }
+        if (!kMagicC || !(rem_m < Q.half_dm && rem_v < Q.thr_v)) {
+            // Rare: codes that fail their check take the reference's
+            // double-precision expression (all of them for 32-bit codes).
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                float rr;
+                round_checked<kCorrect>(__fmul_rn(m[k], Q.rdm), m[k], Q.dm, Q.half_dm, rr);
+                if (!kMagicC || !(rr < Q.half_dm)) mw[k] = CI::m_word(requant_m_ref(m[k], Q.dm, C.lm_d));
+                const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -Q.lmin)
+                                         : __fsub_rn(logf(x[k]), Q.lmin);
+                round_checked<kCorrect>(__fmul_rn(xv, Q.rdv), xv, Q.dv, Q.half_dv, rr);
+                if (!kMagicC || !(rr < Q.thr_v))
+                    vw[k] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[k]), Q.lmin), Q.dv, C.lv_d));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
+            int a4[4], b4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { a4[j] = mw[4 * i + j]; b4[j] = vw[4 * i + j]; }
+            if (FULL) {
+                CI::store4(T, e, a4, b4);
+            } else {
+                const int64_t rem = n - e;
+                const int c = rem >= 4 ? 4 : (rem > 0 ? (int)rem : 0);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < c) CI::store1(T, e + j, a4[j], b4[j]);
+            }
+        }
+    }
+}
+
 // One quantisation block (unit) of the tensor in X, starting at element e0.
 // FULL: all B elements in range and all pointers allow vector access.
 template <int LAYOUT, typename GT, bool EXACT_P, bool FULL, int LOGB, bool TBL, bool GR>
@@ -153,10 +235,12 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                 if constexpr (LAYOUT == MDQ_LAYOUT_PACKED4) {
                     raw[i].w = pre.m[i];   // the packed byte pairs, decoded by table
                 } else {
+                    // int8/uint8 code bytes (the only prefetched plain layout)
+                    const unsigned mw = pre.m[i] ^ 0x80808080u;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        qm[4 * i + j] = (int)(int8_t)(uint8_t)(pre.m[i] >> (8 * j));
-                        qv[4 * i + j] = (int)((pre.v[i] >> (8 * j)) & 0xffu);
+                        m[4 * i + j] = __fmul_rn(byte_as_float_s8(mw, j), sm);
+                        v[4 * i + j] = dequant_v(byte_as_float_u8(pre.v[i], j), sv, vmn);
                     }
                 }
             }
@@ -206,6 +290,8 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                     m[4 * i + j] = TC::m(raw[i], j, tm, sm);
                     v[4 * i + j] = TC::v(raw[i], j, tv);
                 }
+        } else if constexpr (kPre) {
+            // (dequantised above, from the prefetched code bytes)
         } else {
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
@@ -291,63 +377,7 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
     }
 
     // ---- pass 2: requantise (CUDA/stquant_kernel.cu:204-216) ---------------
-    constexpr bool kCorrect = !kApprox;
-#pragma unroll 1
-    for (int s = 0; s < S; ++s) {
-        float m[8], x[8];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int o = 256 * s + 128 * i + 4 * lane;
-            const float4 a = *reinterpret_cast<const float4*>(wm + o);
-            const float4 b = *reinterpret_cast<const float4*>(wx + o);
-            m[4 * i + 0] = a.x; m[4 * i + 1] = a.y; m[4 * i + 2] = a.z; m[4 * i + 3] = a.w;
-            x[4 * i + 0] = b.x; x[4 * i + 1] = b.y; x[4 * i + 2] = b.z; x[4 * i + 3] = b.w;
-        }
-        int mw[8], vw[8];
-        float rem_m = 0.0f, rem_v = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            float rr;
-            mw[k] = min(round_checked<kCorrect, kB>(__fmul_rn(m[k], Q.rdm), m[k], Q.dm,
-                                                    Q.half_dm, rr), Q.mw_hi);
-            rem_m = max_nan(rem_m, rr);
-            const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -Q.lmin)
-                                     : __fsub_rn(logf(x[k]), Q.lmin);
-            vw[k] = round_checked<kCorrect>(__fmul_rn(xv, Q.rdv), xv, Q.dv, Q.half_dv, rr);
-            rem_v = max_nan(rem_v, rr);
-        }
-        if (!kMagicC || !(rem_m < Q.half_dm && rem_v < Q.thr_v)) {
-            // Rare: codes that fail their check take the reference's
-            // double-precision expression (all of them for 32-bit codes).
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                float rr;
-                round_checked<kCorrect>(__fmul_rn(m[k], Q.rdm), m[k], Q.dm, Q.half_dm, rr);
-                if (!kMagicC || !(rr < Q.half_dm)) mw[k] = CI::m_word(requant_m_ref(m[k], Q.dm, C.lm_d));
-                const float xv = kApprox ? __fmaf_rn(approx_log2(x[k]), kLn2, -Q.lmin)
-                                         : __fsub_rn(logf(x[k]), Q.lmin);
-                round_checked<kCorrect>(__fmul_rn(xv, Q.rdv), xv, Q.dv, Q.half_dv, rr);
-                if (!kMagicC || !(rr < Q.thr_v))
-                    vw[k] = CI::v_word(requant_v_ref(__fsub_rn(logf(x[k]), Q.lmin), Q.dv, C.lv_d));
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
-            int a4[4], b4[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) { a4[j] = mw[4 * i + j]; b4[j] = vw[4 * i + j]; }
-            if (FULL) {
-                CI::store4(T, e, a4, b4);
-            } else {
-                const int64_t rem = n - e;
-                const int c = rem >= 4 ? 4 : (rem > 0 ? (int)rem : 0);
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (j < c) CI::store1(T, e + j, a4[j], b4[j]);
-            }
-        }
-    }
+    requant_block<LAYOUT, FULL, LOGB>(X, e0, Q, ParkSplit{wm, wx});
 }
 
 // Partial or unaligned blocks (a tensor's tail) take an out-of-line copy of

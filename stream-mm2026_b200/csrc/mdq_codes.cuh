@@ -42,6 +42,19 @@ __device__ __forceinline__ float small_int_to_float(int q) {
     return __fsub_rn(__int_as_float(kMagicBits + q), kMagic);
 }
 
+// The four byte codes of a word as exact floats, one byte permute each: a
+// byte u placed in the low byte of kMagicBits (whose low byte is zero) is the
+// float 1.5 * 2^23 + u.  int8 codes are biased to u = q + 128 first (one xor
+// per word) and unbiased in the subtraction.
+__device__ __forceinline__ float byte_as_float_u8(unsigned w, int j) {
+    return __fsub_rn(__int_as_float((int)__byte_perm(w, (unsigned)kMagicBits, 0x7650u + (unsigned)j)),
+                     kMagic);
+}
+__device__ __forceinline__ float byte_as_float_s8(unsigned w_xor80, int j) {
+    return __fsub_rn(__int_as_float((int)__byte_perm(w_xor80, (unsigned)kMagicBits, 0x7650u + (unsigned)j)),
+                     kMagic + 128.0f);
+}
+
 // Pointers of the tensor a CTA is working on.
 struct TensorPtrs {
     float* p;

@@ -86,6 +86,74 @@ __device__ __forceinline__ float update_p(float w, float m, float v, const StepC
     }
 }
 
+// ---------------------------------------------------------------------------
+// Element pairs.  sm_100 issues two fp32 adds, multiplies or fused
+// multiply-adds as one instruction on a register pair (add / mul / fma
+// .rn.f32x2); each half is rounded to nearest exactly as the scalar
+// __fadd_rn / __fmul_rn / __fmaf_rn, so the pair forms below return the same
+// bits as their scalar counterparts, for half the issue slots.  Used only
+// where no paired multiply feeds a paired add: ptxas (CUDA 12.9) was observed
+// to fuse mul.rn.f32x2 followed by add.rn.f32x2 into one fused multiply-add,
+// which changes the rounding (the magic-number rounding of the code checks
+// stays scalar for that reason).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 bcast2(float a) { return make_float2(a, a); }
+
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// m = beta1*m + (1-beta1)*g for two elements.
+__device__ __forceinline__ float2 adam_m2(float2 m, float2 g, const StepConsts& c) {
+    return fma2_rn(bcast2(c.b1), m, mul2_rn(bcast2(c.omb1), g));
+}
+
+// v = beta2*v + (1-beta2)*g*g for two elements.
+__device__ __forceinline__ float2 adam_v2(float2 v, float2 g, const StepConsts& c) {
+    return fma2_rn(bcast2(c.b2), v, mul2_rn(mul2_rn(bcast2(c.omb2), g), g));
+}
+
+// Parameter update of two elements (update_p).
+template <bool EXACT>
+__device__ __forceinline__ float2 update_p2(float2 w, float2 m, float2 v, const StepConsts& c) {
+    if (EXACT) {
+        return make_float2(update_p<true>(w.x, m.x, v.x, c), update_p<true>(w.y, m.y, v.y, c));
+    } else {
+        float2 s, r;
+        asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(s.x) : "f"(v.x));
+        asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(s.y) : "f"(v.y));
+        const float2 denom = fma2_rn(s, bcast2(c.inv_sqrt_bc2), bcast2(c.eps));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(denom.x));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(denom.y));
+        if (c.wd != 0.0f) w = mul2_rn(w, bcast2(c.decay));
+        return fma2_rn(bcast2(-c.step_size), mul2_rn(m, r), w);
+    }
+}
+
 // log(v + 1e-12)  (CUDA/stquant_kernel.cu:185).
 __device__ __forceinline__ float log_v_of(float v) { return logf(__fadd_rn(v, 1e-12f)); }
 

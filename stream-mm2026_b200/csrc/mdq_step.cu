@@ -41,6 +41,13 @@
 #include "mdq_tiles.cuh"
 #include "mdq_blocks.cuh"
 
+namespace mdq {
+// Bulk-copy staged warp-per-block kernel, int8/uint8 codes (mdq_staged_s8u8.cu).
+template <int CAP>
+mdq_status launch_staged_s8u8(int gdt, const LaunchParams<CAP>& P, bool exact, int logb, int sms,
+                              cudaStream_t s);
+}  // namespace mdq
+
 // The C layout the Python mirror (mdq_b200/kernels.py, _lib.py) packs.
 static_assert(offsetof(mdq_tensor_desc, grad_dtype) == 104, "mdq_tensor_desc layout");
 static_assert(offsetof(mdq_tensor_desc, p_bf16) == 112, "mdq_tensor_desc layout");
@@ -208,6 +215,13 @@ bool vec_ok(const mdq_tensor_desc& d) {
     return false;
 }
 
+// Bit 1 of LaunchDesc::vec: every streamed array starts on a 16-byte
+// boundary, as bulk copies into shared memory need (int8/uint8 codes).
+bool bulk_ok(const mdq_tensor_desc& d) {
+    return d.layout == MDQ_LAYOUT_S8U8 && aligned(d.p, 16) && aligned(d.grad, 16) &&
+           aligned(d.exp_avg, 16) && aligned(d.exp_avg_sq, 16);
+}
+
 bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
 int ilog2(int x) { int l = 0; while ((1 << l) < x) ++l; return l; }
 
@@ -269,7 +283,7 @@ mdq::LaunchDesc to_launch(const mdq_tensor_desc& d) {
     L.m_bits = (int8_t)d.m_bits;
     L.v_bits = (int8_t)d.v_bits;
     L.log2_block = (int8_t)ilog2(d.block);
-    L.vec = (int8_t)vec_ok(d);
+    L.vec = (int8_t)(vec_ok(d) ? (bulk_ok(d) ? 3 : 1) : 0);
     return L;
 }
 
@@ -327,6 +341,26 @@ bool use_block_kernel(int layout, int block, bool exact) {
     }
     if (mode >= 0) return mode == 1;
     return layout == MDQ_LAYOUT_S8U8 || (layout == MDQ_LAYOUT_PACKED4 && exact && block == 1024);
+}
+
+// Whether int8/uint8 classes on the warp-per-block path take the bulk-copy
+// staged variant (mdq_staged.cuh); it serves launches without peers or
+// gradient ranks.  Measured on B200 (2^30 elements, bf16 gradients,
+// Gparams/s, staged vs direct loads, fast p / exact p):
+//   512-element blocks:  341 vs 239 / 240 vs 187
+//   1024-element blocks: 356 vs 330 / 251 vs 255
+// so exact p at 1024-element blocks stays on the direct kernel.
+// MDQ_STAGED=0 / =1 forces the choice (measurement).  Read once.
+bool use_staged_kernel(int layout, int block, bool exact, const mdq::PeerSet& peers,
+                       const mdq::GradRanks& granks) {
+    static int mode = -2;
+    if (mode == -2) {
+        const char* e = getenv("MDQ_STAGED");
+        mode = e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
+    }
+    if (layout != MDQ_LAYOUT_S8U8 || peers.n != 0 || granks.n != 0) return false;
+    if (mode >= 0) return mode == 1;
+    return !(exact && block == 1024);
 }
 
 template <int CAP>
@@ -419,8 +453,10 @@ mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bo
             }
             P.total_tiles = (int32_t)units;
             const mdq_tensor_desc& d0 = descs[idx[i - 1]];
-            const mdq_status st = launch_blocks<CAP>(d0.layout, d0.grad_dtype, P, exact, logb,
-                                                     sms, s);
+            const mdq_status st =
+                use_staged_kernel(d0.layout, min_block, exact, peers, granks)
+                    ? mdq::launch_staged_s8u8<CAP>(d0.grad_dtype, P, exact, logb, sms, s)
+                    : launch_blocks<CAP>(d0.layout, d0.grad_dtype, P, exact, logb, sms, s);
             if (st != MDQ_OK) return st;
         }
         return MDQ_OK;

@@ -120,6 +120,33 @@ def test_multi_tensor_matches_single(ref, cuda_device):
             assert all(v == 0 for v in mm.values()), f"step {s}: {mm}"
 
 
+@pytest.mark.parametrize("block", [512, 1024])
+@pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16])
+def test_int8_codes_many_tensors(ref, cuda_device, block, gdt):
+    """int8/uint8 codes at 512/1024-element blocks, several tensors in one call:
+    tensors that start and end inside a CTA's share of blocks, tails, a tensor
+    of one block, one shorter than a block, and one whose m codes start 8
+    bytes past a 16-byte boundary (no bulk copies for it) == reference."""
+    sizes = [3 * block, 50 * block + 17, 100, 700 * block, block, 5000, 64 * block + 1]
+    refs = [State(n, block, "s8u8", cuda_device, seed=i) for i, n in enumerate(sizes)]
+    mine = [r.clone() for r in refs]
+    odd = mine[1]
+    buf = torch.empty(odd.n + 8, dtype=odd.m.dtype, device=cuda_device)
+    odd.m = buf[8:8 + odd.n]
+    odd.m.copy_(refs[1].m)
+    for s in range(1, 5):
+        items = []
+        for i, (n, ra, mi) in enumerate(zip(sizes, refs, mine)):
+            g = grads(n, 1, cuda_device, gdt, seed=100 * s + i)[0]
+            run_ref(ref, ra, g, s, 8)
+            items.append(item_of(mi, g, s, 8, 8, LAYOUT_S8U8))
+        kernels.step_multi(items, p_mode=P_EXACT)
+        torch.cuda.synchronize()
+        for i, (ra, mi) in enumerate(zip(refs, mine)):
+            mm = ra.mismatches(mi)
+            assert all(v == 0 for v in mm.values()), f"step {s} tensor {i}: {mm}"
+
+
 def test_many_tensors_one_launch(ref, cuda_device):
     """More descriptors than one launch holds (224) still match."""
     sizes = [(i * 37) % 900 + 1 for i in range(300)]
