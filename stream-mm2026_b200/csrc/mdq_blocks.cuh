@@ -301,11 +301,25 @@ __device__ __forceinline__ void block_body(const TileCtx& X, int64_t e0, float* 
                 v[k] = dequant_v(qvf, sv, vmn);
             }
         }
+        if constexpr (EXACT_P) {
+            // (scalar: measured faster than pairs with the IEEE divides)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            m[k] = adam_m(m[k], g[k], C);
-            v[k] = adam_v(v[k], g[k], C);
-            p[k] = update_p<EXACT_P>(p[k], m[k], v[k], C);
+            for (int k = 0; k < 8; ++k) {
+                m[k] = adam_m(m[k], g[k], C);
+                v[k] = adam_v(v[k], g[k], C);
+                p[k] = update_p<true>(p[k], m[k], v[k], C);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {   // element pairs (mdq_math.cuh)
+                const float2 gg = make_float2(g[k], g[k + 1]);
+                const float2 mm = adam_m2(make_float2(m[k], m[k + 1]), gg, C);
+                const float2 vv = adam_v2(make_float2(v[k], v[k + 1]), gg, C);
+                const float2 pp = update_p2<false>(make_float2(p[k], p[k + 1]), mm, vv, C);
+                m[k] = mm.x; m[k + 1] = mm.y;
+                v[k] = vv.x; v[k + 1] = vv.y;
+                p[k] = pp.x; p[k + 1] = pp.y;
+            }
         }
 #pragma unroll
         for (int i = 0; i < 2; ++i) {

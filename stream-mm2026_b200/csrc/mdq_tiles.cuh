@@ -381,24 +381,46 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
                 m[4 * i + j] = TC::m(raw[i], j, tm, sm);
                 v[4 * i + j] = TC::v(raw[i], j, tv);
             }
+    } else if constexpr (kMagicC) {
+        // Element pairs: the magic-word subtraction, the scale multiply and
+        // the exponent's fused multiply-add as paired instructions.
+#pragma unroll
+        for (int k = 0; k < PT; k += 2) {
+            const float2 qmf = add2_rn(make_float2(__int_as_float(kMagicBits + qm[k]),
+                                                   __int_as_float(kMagicBits + qm[k + 1])),
+                                       bcast2(-kMagic));
+            const float2 mm = mul2_rn(qmf, bcast2(sm));
+            const float2 qvf = add2_rn(make_float2(__int_as_float(kMagicBits + qv[k]),
+                                                   __int_as_float(kMagicBits + qv[k + 1])),
+                                       bcast2(-kMagic));
+            const float2 ev = fma2_rn(qvf, bcast2(sv), bcast2(vmn));
+            m[k] = mm.x; m[k + 1] = mm.y;
+            v[k] = expf(ev.x); v[k + 1] = expf(ev.y);
+        }
     } else {
 #pragma unroll
         for (int k = 0; k < PT; ++k) {
-            const float qmf = kMagicC ? small_int_to_float(qm[k]) : (float)qm[k];
-            m[k] = __fmul_rn(qmf, sm);
-            const float qvf = kMagicC ? small_int_to_float(qv[k]) : (float)(unsigned)qv[k];
-            v[k] = dequant_v(qvf, sv, vmn);
+            m[k] = __fmul_rn((float)qm[k], sm);
+            v[k] = dequant_v((float)(unsigned)qv[k], sv, vmn);
         }
     }
     if (PROF && tid == 0) prof_mark(pc, 0, t0);
+    // AdamW moments and the parameter update on element pairs (mdq_math.cuh).
 #pragma unroll
-    for (int k = 0; k < PT; ++k) {
-        m[k] = adam_m(m[k], g[k], C);
-        v[k] = adam_v(v[k], g[k], C);
+    for (int k = 0; k < PT; k += 2) {
+        const float2 gg = make_float2(g[k], g[k + 1]);
+        const float2 mm = adam_m2(make_float2(m[k], m[k + 1]), gg, C);
+        const float2 vv = adam_v2(make_float2(v[k], v[k + 1]), gg, C);
+        m[k] = mm.x; m[k + 1] = mm.y;
+        v[k] = vv.x; v[k + 1] = vv.y;
     }
     if (PROF && tid == 0) prof_mark(pc, 1, t0);
 #pragma unroll
-    for (int k = 0; k < PT; ++k) p[k] = update_p<EXACT_P>(p[k], m[k], v[k], C);
+    for (int k = 0; k < PT; k += 2) {
+        const float2 pp = update_p2<EXACT_P>(make_float2(p[k], p[k + 1]), make_float2(m[k], m[k + 1]),
+                                             make_float2(v[k], v[k + 1]), C);
+        p[k] = pp.x; p[k + 1] = pp.y;
+    }
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
         const int64_t e = e_first + (int64_t)cstride * i;
@@ -458,8 +480,16 @@ __device__ __forceinline__ void tile_body(const TileCtx& X, int64_t tile_e0,
     // reference's reduction does; elements past the end enter as |m| = 0 and
     // x = 1 (log v = 0, :92-93).
     float x[PT];
+    if (FULL) {
 #pragma unroll
-    for (int k = 0; k < PT; ++k) x[k] = (FULL || (k & 3) < cnt[k / 4]) ? __fadd_rn(v[k], 1e-12f) : 1.0f;
+        for (int k = 0; k < PT; k += 2) {
+            const float2 xx = add2_rn(make_float2(v[k], v[k + 1]), bcast2(1e-12f));
+            x[k] = xx.x; x[k + 1] = xx.y;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < PT; ++k) x[k] = (k & 3) < cnt[k / 4] ? __fadd_rn(v[k], 1e-12f) : 1.0f;
+    }
     float s0 = kNaN, s1 = kNaN, s2 = kNaN;
 #pragma unroll
     for (int k = 0; k < PT; k += 2) {
