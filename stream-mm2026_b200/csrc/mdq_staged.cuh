@@ -1,5 +1,5 @@
 // mdq_staged.cuh - warp-per-block fused step with bulk-copy (TMA) staging,
-// for int8/uint8 codes and quantisation blocks of 512 or 1024 elements.
+// for int8/uint8 codes and quantisation blocks of 128 to 1024 elements.
 //
 // The warp-per-block kernel (mdq_blocks.cuh) loads each sub-tile with plain
 // per-lane loads one sub-tile ahead; with 16 warps per SM that keeps about
@@ -31,22 +31,31 @@ namespace mdq {
 constexpr int kChunkLog = 9;                 // 512-element chunks
 constexpr int kChunk = 1 << kChunkLog;
 
-template <int LOGB> __host__ __device__ constexpr int stg_cpb() { return 1 << (LOGB - kChunkLog); }
+// A warp's unit of work: one block of 2^LOGB elements (LOGB >= 9), or, for
+// blocks of 128 or 256 elements, 1024 elements (8 or 4 whole blocks).
+template <int LOGB> __host__ __device__ constexpr int stg_logu() { return LOGB >= 9 ? LOGB : 10; }
+template <int LOGB> __host__ __device__ constexpr int stg_cpb() { return 1 << (stg_logu<LOGB>() - kChunkLog); }
 template <int LOGB> __host__ __device__ constexpr int stg_ns() { return stg_cpb<LOGB>() + 1; }
 template <typename GT> __host__ __device__ constexpr int stg_chunk_bytes() {
     return (4 + (int)sizeof(GT) + 2) * kChunk;
 }
+// Blocks of a unit; with small blocks a unit's first chunk slot also holds
+// the blocks' old scales (sm, sv, v_min: three 32-byte areas behind it).
+template <int LOGB> __host__ __device__ constexpr int stg_nbu() { return 1 << (stg_logu<LOGB>() - LOGB); }
+template <typename GT, int LOGB> __host__ __device__ constexpr int stg_slot_bytes() {
+    return stg_chunk_bytes<GT>() + (LOGB >= 9 ? 0 : 128);
+}
 // Warps per CTA and resident CTAs per SM: 8 warps and 2 CTAs (16 warps per
 // SM at up to 128 registers) when the ring fits twice per SM, else 4 warps
-// and 3 CTAs (fp32 gradients at 1024-element blocks: 15 KB per warp).
+// and 3 CTAs (fp32 gradients at 1024-element units: 15 KB per warp).
 template <typename GT, int LOGB> __host__ __device__ constexpr int stg_warps() {
-    return 8 * stg_ns<LOGB>() * stg_chunk_bytes<GT>() <= 100 * 1024 ? 8 : 4;
+    return 8 * stg_ns<LOGB>() * stg_slot_bytes<GT, LOGB>() <= 100 * 1024 ? 8 : 4;
 }
 template <typename GT, int LOGB> __host__ __device__ constexpr int stg_min_ctas() {
     return stg_warps<GT, LOGB>() == 8 ? 2 : 3;
 }
 template <typename GT, int LOGB> __host__ __device__ constexpr int stg_smem_bytes() {
-    return stg_warps<GT, LOGB>() * stg_ns<LOGB>() * stg_chunk_bytes<GT>();
+    return stg_warps<GT, LOGB>() * stg_ns<LOGB>() * stg_slot_bytes<GT, LOGB>();
 }
 
 // Iteration limit of a wait on a slot's mbarrier.  A bulk copy of a few KB
@@ -93,22 +102,31 @@ __device__ __forceinline__ void bulk_load(unsigned dst, const void* src, unsigne
         : "memory");
 }
 
-// Issues the copies of chunk c of the block at element e0 of tensor T into
-// the slot at shared address `dst` (lane 0 only).  Every lane must have
-// finished its accesses of the slot and fenced them against the async proxy
-// before.
+// Issues the copies of the chunk at element e0 of tensor T into the slot at
+// shared address `dst` (lane 0 only); with `nsc` > 0 also the old scales of
+// the nsc blocks from block blk0 on, behind the chunk (32-byte areas).  Every
+// lane must have finished its accesses of the slot and fenced them against
+// the async proxy before.
 template <typename GT>
 __device__ __forceinline__ void stage_chunk(const TensorPtrs& T, int64_t e0, unsigned dst,
-                                            unsigned bar, unsigned long long policy) {
+                                            unsigned bar, unsigned long long policy,
+                                            int64_t blk0 = 0, int nsc = 0) {
     constexpr unsigned C = kChunk;
     constexpr unsigned kG = (unsigned)sizeof(GT) * C;
+    const unsigned sb = 4u * (unsigned)nsc;
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                 "r"((unsigned)stg_chunk_bytes<GT>())
+                 "r"((unsigned)stg_chunk_bytes<GT>() + 3 * sb)
                  : "memory");
     bulk_load(dst, T.p + e0, 4 * C, bar, policy);
     bulk_load(dst + 4 * C, static_cast<const GT*>(T.g) + e0, kG, bar, policy);
     bulk_load(dst + 4 * C + kG, static_cast<const int8_t*>(T.m) + e0, C, bar, policy);
     bulk_load(dst + 5 * C + kG, static_cast<const uint8_t*>(T.v) + e0, C, bar, policy);
+    if (nsc > 0) {
+        const unsigned so = (unsigned)stg_chunk_bytes<GT>();
+        bulk_load(dst + so, T.sm + blk0, sb, bar, policy);
+        bulk_load(dst + so + 32, T.sv + blk0, sb, bar, policy);
+        bulk_load(dst + so + 64, T.vmin + blk0, sb, bar, policy);
+    }
 }
 
 // Park addresses inside consumed chunks; sub-tile s of the block lies in
@@ -269,7 +287,186 @@ __device__ __forceinline__ bool staged_block_body(const TileCtx& X, int64_t e0,
     return true;
 }
 
-// Persistent grid: CTA c takes units (blocks) [total c / grid,
+// One full, staged unit of 1024 elements holding NBU = 1024 / B whole blocks
+// of B = 128 or 256 elements.  Sub-tile s (256 elements) holds blocks
+// (2 s, 2 s + 1) (B = 128: its halves i = 0, 1) or block s (B = 256); every
+// lane has 4 elements of each block it touches.  Pass 1 runs as for large
+// blocks, with the block's old scales read from the unit's staged scale areas;
+// each block's three extremes are reduced over the warp right after its
+// sub-tile and kept by lane b = block index.  Then every lane evaluates the
+// requantisation constants of block `lane` (one evaluation per lane covers
+// all NBU blocks, instead of one per lane and block), lanes < NBU store the
+// new scales, and pass 2 takes each block's constants from lane b by shuffle.
+// Returns false when a wait ran out.
+template <typename GT, bool EXACT_P, int LOGB>
+__device__ __forceinline__ bool staged_small_body(const TileCtx& X, int64_t e0,
+                                                  const ParkRing<GT, 2>& park,
+                                                  const unsigned (&bars)[2],
+                                                  const unsigned (&par)[2]) {
+    using CI = Codes<MDQ_LAYOUT_S8U8>;
+    constexpr int C = kChunk;
+    constexpr int kG = (int)sizeof(GT) * C;
+    constexpr int NBU = stg_nbu<LOGB>();
+    const float kNaN = __int_as_float(0x7fffffff);
+    const int lane = threadIdx.x & 31;
+    const TensorPtrs T = X.t;
+    const StepConsts& Cs = X.C;
+    const int64_t blk0 = e0 >> LOGB;
+    const float* scl = reinterpret_cast<const float*>(park.ch[0] + stg_chunk_bytes<GT>());
+    float R0 = kNaN, R1 = kNaN, R2 = kNaN;   // this lane's block (lane < NBU): extremes
+
+    // ---- pass 1 (:163-199) -------------------------------------------------
+#pragma unroll 1
+    for (int s = 0; s < 4; ++s) {
+        if ((s & 1) == 0) {
+            const unsigned bar = s == 0 ? bars[0] : bars[1];
+            const unsigned ph = s == 0 ? par[0] : par[1];
+            if (!mbar_wait(bar, ph)) return false;
+        }
+        const char* chunk = park.chunk(s >> 1);
+        const int t = s & 1;
+        float2 p[4], g[4], m[4], v[4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int b = LOGB == 7 ? 2 * s + i : s;          // block within the unit
+            const float sm = scl[b], sv = scl[8 + b], vmn = scl[16 + b];
+            const int k = 256 * t + 128 * i + 4 * lane;
+            const float4 a = *reinterpret_cast<const float4*>(chunk + 4 * k);
+            p[2 * i] = make_float2(a.x, a.y);
+            p[2 * i + 1] = make_float2(a.z, a.w);
+            float gg[4];
+            const typename GradRaw<GT>::T gw =
+                *reinterpret_cast<const typename GradRaw<GT>::T*>(chunk + 4 * C + (int)sizeof(GT) * k);
+            GradRaw<GT>::decode(gw, gg);
+            g[2 * i] = make_float2(gg[0], gg[1]);
+            g[2 * i + 1] = make_float2(gg[2], gg[3]);
+            const unsigned mw = *reinterpret_cast<const unsigned*>(chunk + 4 * C + kG + k) ^ 0x80808080u;
+            const unsigned vw = *reinterpret_cast<const unsigned*>(chunk + 5 * C + kG + k);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float2 qm = add2_rn(
+                    make_float2(__int_as_float((int)__byte_perm(mw, (unsigned)kMagicBits, 0x7650u + 2 * h)),
+                                __int_as_float((int)__byte_perm(mw, (unsigned)kMagicBits, 0x7651u + 2 * h))),
+                    bcast2(-(kMagic + 128.0f)));
+                const float2 qv = add2_rn(
+                    make_float2(__int_as_float((int)__byte_perm(vw, (unsigned)kMagicBits, 0x7650u + 2 * h)),
+                                __int_as_float((int)__byte_perm(vw, (unsigned)kMagicBits, 0x7651u + 2 * h))),
+                    bcast2(-kMagic));
+                m[2 * i + h] = mul2_rn(qm, bcast2(sm));
+                const float2 ev = fma2_rn(qv, bcast2(sv), bcast2(vmn));
+                v[2 * i + h] = make_float2(expf(ev.x), expf(ev.y));
+            }
+        }
+        __syncwarp();   // every lane's reads of this sub-tile precede the parks
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            m[k] = adam_m2(m[k], g[k], Cs);
+            v[k] = adam_v2(v[k], g[k], Cs);
+            p[k] = update_p2<EXACT_P>(p[k], m[k], v[k], Cs);
+        }
+        float2 x[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = add2_rn(v[k], bcast2(1e-12f));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int64_t e = e0 + 256 * s + 128 * i + 4 * lane;
+            const float4 pv = make_float4(p[2 * i].x, p[2 * i].y, p[2 * i + 1].x, p[2 * i + 1].y);
+            __stcs(reinterpret_cast<float4*>(T.p + e), pv);
+            if (T.p16 != nullptr) {
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(pv.x, pv.y);
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(pv.z, pv.w);
+                uint2 w;
+                w.x = *reinterpret_cast<const unsigned*>(&lo);
+                w.y = *reinterpret_cast<const unsigned*>(&hi);
+                __stcs(reinterpret_cast<uint2*>(T.p16 + e), w);
+            }
+            *reinterpret_cast<float4*>(park.m(s, i, lane)) =
+                make_float4(m[2 * i].x, m[2 * i].y, m[2 * i + 1].x, m[2 * i + 1].y);
+            *reinterpret_cast<float4*>(park.x(s, i, lane)) =
+                make_float4(x[2 * i].x, x[2 * i].y, x[2 * i + 1].x, x[2 * i + 1].y);
+        }
+        // Block extremes (:184-199), reduced over the warp per block.
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            if (LOGB == 8 && i == 1) break;
+            const int k0 = LOGB == 7 ? 2 * i : 0, k1 = LOGB == 7 ? 2 * i + 2 : 4;
+            float a0 = kNaN, a1 = kNaN, a2 = kNaN;
+#pragma unroll
+            for (int k = k0; k < k1; ++k) {
+                a0 = max3f(a0, fabsf(m[k].x), fabsf(m[k].y));
+                a1 = max3f(a1, x[k].x, x[k].y);
+                a2 = min3f(a2, x[k].x, x[k].y);
+            }
+            asm volatile("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(a0));
+            asm volatile("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(a1));
+            asm volatile("redux.sync.min.f32 %0, %0, 0xffffffff;" : "+f"(a2));
+            const int b = LOGB == 7 ? 2 * s + i : s;
+            if (lane == b) { R0 = a0; R1 = a1; R2 = a2; }
+        }
+    }
+    __syncwarp();   // parks of other lanes (the bf16 x areas mix lanes)
+    // Constants of block `lane` (lanes >= NBU evaluate a NaN block, unused).
+    const QConsts Q = make_q<CI::kApproxLog, CI::kMBias>(R0, R1, R2, Cs);
+    if (lane < NBU) {
+        T.sm[blk0 + lane] = Q.new_sm;
+        T.sv[blk0 + lane] = Q.new_sv;
+        T.vmin[blk0 + lane] = Q.lmin;
+    }
+
+    // ---- pass 2: requantise (:204-216) -------------------------------------
+#pragma unroll 1
+    for (int s = 0; s < 4; ++s) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int b = LOGB == 7 ? 2 * s + i : s;
+            QConsts q;
+            q.rdm = __shfl_sync(0xffffffffu, Q.rdm, b);
+            q.dm = __shfl_sync(0xffffffffu, Q.dm, b);
+            q.half_dm = __shfl_sync(0xffffffffu, Q.half_dm, b);
+            q.lmin = __shfl_sync(0xffffffffu, Q.lmin, b);
+            q.rdv = __shfl_sync(0xffffffffu, Q.rdv, b);
+            q.dv = __shfl_sync(0xffffffffu, Q.dv, b);
+            q.half_dv = __shfl_sync(0xffffffffu, Q.half_dv, b);
+            q.thr_v = __shfl_sync(0xffffffffu, Q.thr_v, b);
+            q.mw_hi = Q.mw_hi;   // the same for every block
+            const float4 am = *reinterpret_cast<const float4*>(park.m(s, i, lane));
+            const float4 ax = *reinterpret_cast<const float4*>(park.x(s, i, lane));
+            const float mm[4] = {am.x, am.y, am.z, am.w};
+            const float xx[4] = {ax.x, ax.y, ax.z, ax.w};
+            int mw[4], vw[4];
+            float rem_m = 0.0f, rem_v = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float rr;
+                mw[j] = min(round_checked<false, CI::kMBias>(__fmul_rn(mm[j], q.rdm), mm[j], q.dm,
+                                                              q.half_dm, rr), q.mw_hi);
+                rem_m = max_nan(rem_m, rr);
+                const float xv = __fmaf_rn(approx_log2(xx[j]), kLn2, -q.lmin);
+                vw[j] = round_checked<false>(__fmul_rn(xv, q.rdv), xv, q.dv, q.half_dv, rr);
+                rem_v = max_nan(rem_v, rr);
+            }
+            if (!(rem_m < q.half_dm && rem_v < q.thr_v)) {
+                // Rare: codes that fail their check take the reference's
+                // double-precision expression.
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float rr;
+                    round_checked<false>(__fmul_rn(mm[j], q.rdm), mm[j], q.dm, q.half_dm, rr);
+                    if (!(rr < q.half_dm)) mw[j] = CI::m_word(requant_m_ref(mm[j], q.dm, Cs.lm_d));
+                    const float xv = __fmaf_rn(approx_log2(xx[j]), kLn2, -q.lmin);
+                    round_checked<false>(__fmul_rn(xv, q.rdv), xv, q.dv, q.half_dv, rr);
+                    if (!(rr < q.thr_v))
+                        vw[j] = CI::v_word(requant_v_ref(__fsub_rn(logf(xx[j]), q.lmin), q.dv, Cs.lv_d));
+                }
+            }
+            CI::store4(T, e0 + 256 * s + 128 * i + 4 * lane, mw, vw);
+        }
+    }
+    return true;
+}
+
+// Persistent grid: CTA c takes units (one block, or 1024 elements of small
+// blocks) [total c / grid,
 // total (c + 1) / grid), warp w the units lo + w, lo + w + W, ...  A unit is
 // staged when its tensor allows bulk copies (16-byte aligned bases, bit 1 of
 // `vec`) and the block is full.  The chunks of unit u sit at ring positions
@@ -283,9 +480,14 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
     constexpr int W = stg_warps<GT, LOGB>();
     constexpr int CPB = stg_cpb<LOGB>();
     constexpr int NS = stg_ns<LOGB>();
-    constexpr int kCh = stg_chunk_bytes<GT>();
+    constexpr int kCh = stg_slot_bytes<GT, LOGB>();
     constexpr int B = 1 << LOGB;
-    static_assert(NS * kCh >= 2 * B * (int)sizeof(float), "the ring holds a direct-path park");
+    constexpr int LOGU = stg_logu<LOGB>();
+    constexpr int U = 1 << LOGU;              // elements of a unit
+    constexpr int NBU = stg_nbu<LOGB>();
+    constexpr bool kSmall = LOGB < 9;
+    static_assert(kSmall || NS * kCh >= 2 * B * (int)sizeof(float),
+                  "the ring holds a direct-path park");
     extern __shared__ __align__(128) char s_ring[];
     __shared__ TileCtx s_wctx[W];
     __shared__ __align__(8) unsigned long long s_bar[W][NS];
@@ -337,7 +539,7 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
                 X.t = D.t;
                 X.n = D.n;
                 X.tile_begin = D.tile_begin;
-                X.tile_end = D.tile_begin + (int32_t)((D.n + B - 1) >> LOGB);
+                X.tile_end = D.tile_begin + (int32_t)((D.n + U - 1) >> LOGU);
                 X.lb = LOGB;
                 X.vec = D.vec;
                 X.C = make_step_consts(D.b1, D.b2, D.lr, D.wd, D.eps, D.step, D.m_bits,
@@ -347,11 +549,11 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
             cur_end = X.tile_end;
         }
         const bool bulk = (X.vec & 2) != 0;
-        const int64_t e0 = (int64_t)(u - X.tile_begin) << LOGB;
-        const bool stage_cur = bulk && e0 + B <= X.n;
+        const int64_t e0 = (int64_t)(u - X.tile_begin) << LOGU;
+        const bool stage_cur = bulk && e0 + U <= X.n;
         const int u2 = u + W;
-        const int64_t e2 = (int64_t)(u2 - X.tile_begin) << LOGB;
-        const bool stage_next = bulk && u2 < hi && u2 < cur_end && e2 + B <= X.n;
+        const int64_t e2 = (int64_t)(u2 - X.tile_begin) << LOGU;
+        const bool stage_next = bulk && u2 < hi && u2 < cur_end && e2 + U <= X.n;
         // Every lane is done with the free slots (earlier units); order those
         // generic accesses before the copy engine writes them.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -367,17 +569,25 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
             par[c] = (parity >> pos[c]) & 1u;
             if (stage_cur && held_at(pos[c]) != u * CPB + c) {
                 if (lane == 0)
-                    stage_chunk<GT>(X.t, e0 + c * kChunk, ring_s + pos[c] * kCh, bars[c], policy);
+                    stage_chunk<GT>(X.t, e0 + c * kChunk, ring_s + pos[c] * kCh, bars[c], policy,
+                                    e0 >> LOGB, kSmall && c == 0 ? NBU : 0);
                 set_held(pos[c], u * CPB + c);
             }
         }
         const int fpos = base + CPB >= NS ? base + CPB - NS : base + CPB;   // the free slot
         if (stage_next) {
-            if (lane == 0) stage_chunk<GT>(X.t, e2, ring_s + fpos * kCh, bar0 + 8 * fpos, policy);
+            if (lane == 0)
+                stage_chunk<GT>(X.t, e2, ring_s + fpos * kCh, bar0 + 8 * fpos, policy, e2 >> LOGB,
+                                kSmall ? NBU : 0);
             set_held(fpos, u2 * CPB);
         }
         if (stage_cur) {
-            if (!staged_block_body<GT, EXACT_P, LOGB>(X, e0, park, bars, par)) {
+            bool ok;
+            if constexpr (kSmall)
+                ok = staged_small_body<GT, EXACT_P, LOGB>(X, e0, park, bars, par);
+            else
+                ok = staged_block_body<GT, EXACT_P, LOGB>(X, e0, park, bars, par);
+            if (!ok) {
                 if (lane == 0) atomicAdd(&g_stage_timeouts, 1u);
                 // Wait, again bounded, for every copy still owed to this
                 // warp's slots before the warp gives up.
@@ -391,7 +601,7 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
                 parity ^= 1u << pos[c];
                 set_held(pos[c], -1);
             }
-        } else {
+        } else if constexpr (!kSmall) {
             // Tails and tensors whose bases do not allow bulk copies (rare):
             // the out-of-line direct-load body, parking at the start of the
             // warp's ring (2 B floats <= NS chunks).  No copy is in flight
@@ -401,6 +611,8 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
             block_body_tail<MDQ_LAYOUT_S8U8, GT, EXACT_P, LOGB, false, false>(
                 X, e0, wm, wm + B);
         }
+        // (Small blocks: the host passes only whole, bulk-aligned units; the
+        // rest of a tensor goes to the tiled kernel.)
         // The remaining chunks of the next unit go into this unit's first
         // slots, now free.
         if (stage_next && CPB > 1) {

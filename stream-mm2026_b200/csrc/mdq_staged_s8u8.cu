@@ -7,18 +7,21 @@ namespace mdq {
 template <int CAP>
 mdq_status launch_staged_s8u8(int gdt, const LaunchParams<CAP>& P, bool exact, int logb, int sms,
                               cudaStream_t s) {
-    if (gdt == MDQ_BF16) {
-        if (logb == 10)
-            return exact ? launch_staged_t<__nv_bfloat16, true, CAP, 10>(P, sms, s)
-                         : launch_staged_t<__nv_bfloat16, false, CAP, 10>(P, sms, s);
-        return exact ? launch_staged_t<__nv_bfloat16, true, CAP, 9>(P, sms, s)
-                     : launch_staged_t<__nv_bfloat16, false, CAP, 9>(P, sms, s);
+#define MDQ_STAGED_CASE(L)                                                                   \
+    case L:                                                                                  \
+        if (gdt == MDQ_BF16)                                                                 \
+            return exact ? launch_staged_t<__nv_bfloat16, true, CAP, L>(P, sms, s)            \
+                         : launch_staged_t<__nv_bfloat16, false, CAP, L>(P, sms, s);          \
+        return exact ? launch_staged_t<float, true, CAP, L>(P, sms, s)                        \
+                     : launch_staged_t<float, false, CAP, L>(P, sms, s);
+    switch (logb) {
+        MDQ_STAGED_CASE(7)
+        MDQ_STAGED_CASE(8)
+        MDQ_STAGED_CASE(9)
+        MDQ_STAGED_CASE(10)
     }
-    if (logb == 10)
-        return exact ? launch_staged_t<float, true, CAP, 10>(P, sms, s)
-                     : launch_staged_t<float, false, CAP, 10>(P, sms, s);
-    return exact ? launch_staged_t<float, true, CAP, 9>(P, sms, s)
-                 : launch_staged_t<float, false, CAP, 9>(P, sms, s);
+#undef MDQ_STAGED_CASE
+    return mdq_fail(MDQ_ERR_INVALID_ARG, "staged kernel: block 2^%d", logb);
 }
 
 template mdq_status launch_staged_s8u8<kCapSmall>(int, const LaunchParams<kCapSmall>&, bool, int,

@@ -33,6 +33,7 @@
 #include <stddef.h>
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "mdq.h"
 #include "mdq_math.cuh"
@@ -349,7 +350,11 @@ bool use_block_kernel(int layout, int block, bool exact) {
 // Gparams/s, staged vs direct loads, fast p / exact p):
 //   512-element blocks:  341 vs 239 / 240 vs 187
 //   1024-element blocks: 356 vs 330 / 251 vs 255
-// so exact p at 1024-element blocks stays on the direct kernel.
+// and, against the tiled kernel, for 128 / 256-element blocks (1024-element
+// units of whole blocks):
+//   128-element blocks:  314 vs 303 / 224 vs 238
+//   256-element blocks:  325 vs 306 / 226 vs 244
+// so exact p at 128, 256 and 1024-element blocks stays on the other kernels.
 // MDQ_STAGED=0 / =1 forces the choice (measurement).  Read once.
 bool use_staged_kernel(int layout, int block, bool exact, const mdq::PeerSet& peers,
                        const mdq::GradRanks& granks) {
@@ -360,7 +365,7 @@ bool use_staged_kernel(int layout, int block, bool exact, const mdq::PeerSet& pe
     }
     if (layout != MDQ_LAYOUT_S8U8 || peers.n != 0 || granks.n != 0) return false;
     if (mode >= 0) return mode == 1;
-    return !(exact && block == 1024);
+    return !(exact && (block == 1024 || block <= 256));
 }
 
 template <int CAP>
@@ -416,10 +421,35 @@ mdq_status launch_tree(const mdq_tensor_desc& d, bool exact, unsigned long long*
 
 // Packs the fast-path descriptors of one (layout, grad dtype) class into
 // launches of at most CAP descriptors each.
+// Small-block staging (blocks of 128 / 256 elements, mdq_staged.cuh) takes
+// whole 1024-element units of tensors whose arrays, scales included, all
+// start on 16-byte boundaries.
+bool bulk_ok_small(const mdq_tensor_desc& d) {
+    return bulk_ok(d) && aligned(d.scale_m, 16) && aligned(d.scale_v, 16) && aligned(d.v_min, 16);
+}
+
+// The same int8/uint8 tensor from element `off` on (a multiple of its block).
+mdq_tensor_desc desc_from(const mdq_tensor_desc& d, int64_t off) {
+    mdq_tensor_desc r = d;
+    const int64_t gsz = d.grad_dtype == MDQ_BF16 ? 2 : 4;
+    r.p = d.p + off;
+    r.grad = static_cast<const char*>(d.grad) + off * gsz;
+    r.exp_avg = static_cast<char*>(d.exp_avg) + off * storage_bits_m(d.layout) / 8;
+    if (d.exp_avg_sq != nullptr)
+        r.exp_avg_sq = static_cast<char*>(d.exp_avg_sq) + off * storage_bits_v(d.layout) / 8;
+    r.scale_m = d.scale_m + off / d.block;
+    r.scale_v = d.scale_v + off / d.block;
+    r.v_min = d.v_min + off / d.block;
+    if (d.p_bf16 != nullptr) r.p_bf16 = static_cast<uint16_t*>(d.p_bf16) + off;
+    r.n = d.n - off;
+    return r;
+}
+
 template <int CAP>
 mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bool exact,
                      unsigned long long* prof, const mdq::PeerSet& peers,
-                     const mdq::GradRanks& granks, int sms, cudaStream_t s) {
+                     const mdq::GradRanks& granks, int sms, cudaStream_t s,
+                     bool allow_small_staged = true) {
     static thread_local mdq::LaunchParams<CAP> P;  // ~24 KB for CAP = 224
     P.peers = peers;
     P.granks = granks;
@@ -432,6 +462,52 @@ mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bo
         max_block = std::max(max_block, (int)descs[idx[k]].block);
     }
     const int layout = descs[idx[0]].layout;
+    if (allow_small_staged && min_block == max_block && (min_block == 128 || min_block == 256) &&
+        prof == nullptr && use_staged_kernel(layout, min_block, exact, peers, granks)) {
+        // Whole 1024-element units of aligned tensors: the staged kernel;
+        // the rest (each tensor's last n mod 1024 elements, which start on a
+        // block boundary, and unaligned tensors): the tiled kernel.
+        constexpr int64_t kUnit = 1024;
+        const int logb = min_block == 128 ? 7 : 8;
+        std::vector<mdq_tensor_desc> rest;
+        std::vector<int> staged;
+        for (int k = 0; k < count; ++k) {
+            const mdq_tensor_desc& d = descs[idx[k]];
+            const int64_t whole = d.n / kUnit * kUnit;
+            if (whole > 0 && bulk_ok_small(d)) {
+                staged.push_back(idx[k]);
+                if (d.n > whole) rest.push_back(desc_from(d, whole));
+            } else {
+                rest.push_back(d);
+            }
+        }
+        size_t i = 0;
+        while (i < staged.size()) {
+            P.n_desc = 0;
+            P.prof = nullptr;
+            int64_t units = 0;
+            while (i < staged.size() && P.n_desc < CAP) {
+                const mdq_tensor_desc& d = descs[staged[i]];
+                const int64_t u = d.n / kUnit;
+                if (units + u > (int64_t)INT32_MAX && P.n_desc > 0) break;
+                mdq::LaunchDesc L = to_launch(d);
+                L.n = u * kUnit;
+                L.tile_begin = (int32_t)units;
+                P.d[P.n_desc++] = L;
+                units += u;
+                ++i;
+            }
+            P.total_tiles = (int32_t)units;
+            const mdq_status st = mdq::launch_staged_s8u8<CAP>(descs[staged[0]].grad_dtype, P,
+                                                               exact, logb, sms, s);
+            if (st != MDQ_OK) return st;
+        }
+        if (rest.empty()) return MDQ_OK;
+        std::vector<int> ridx(rest.size());
+        for (size_t k = 0; k < rest.size(); ++k) ridx[k] = (int)k;
+        return run_class<CAP>(rest.data(), ridx.data(), (int)rest.size(), exact, prof, peers,
+                              granks, sms, s, false);
+    }
     if (min_block == max_block && (min_block == 512 || min_block == 1024) && prof == nullptr &&
         use_block_kernel(layout, min_block, exact)) {
         // Warp-per-block kernel: a launch's units are quantisation blocks.

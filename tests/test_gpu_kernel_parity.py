@@ -120,10 +120,12 @@ def test_multi_tensor_matches_single(ref, cuda_device):
             assert all(v == 0 for v in mm.values()), f"step {s}: {mm}"
 
 
-@pytest.mark.parametrize("block", [512, 1024])
+@pytest.mark.parametrize("block", [128, 256, 512, 1024])
 @pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16])
 def test_int8_codes_many_tensors(ref, cuda_device, block, gdt):
-    """int8/uint8 codes at 512/1024-element blocks, several tensors in one call:
+    """int8/uint8 codes at 128..1024-element blocks (the staged kernels; at 128
+    and 256 each tensor's last n mod 1024 elements go to the tiled kernel),
+    several tensors in one call:
     tensors that start and end inside a CTA's share of blocks, tails, a tensor
     of one block, one shorter than a block, and one whose m codes start 8
     bytes past a 16-byte boundary (no bulk copies for it) == reference."""
