@@ -39,6 +39,11 @@ template <int LOGB> __host__ __device__ constexpr int stg_ns() { return stg_cpb<
 template <typename GT> __host__ __device__ constexpr int stg_chunk_bytes() {
     return (4 + (int)sizeof(GT) + 2) * kChunk;
 }
+// Bytes a chunk's copies bring: int8/uint8 codes two arrays, packed 4-bit
+// codes one (the slot keeps room for two: the park needs 8 B per element).
+template <typename GT, int LAYOUT> __host__ __device__ constexpr int stg_copy_bytes() {
+    return (4 + (int)sizeof(GT) + (LAYOUT == MDQ_LAYOUT_PACKED4 ? 1 : 2)) * kChunk;
+}
 // Blocks of a unit; with small blocks a unit's first chunk slot also holds
 // the blocks' old scales (sm, sv, v_min: three 32-byte areas behind it).
 template <int LOGB> __host__ __device__ constexpr int stg_nbu() { return 1 << (stg_logu<LOGB>() - LOGB); }
@@ -65,6 +70,8 @@ constexpr int kStageWaitLimit = 1 << 22;
 
 // Count of staged-kernel waits that ran out (a warp stops at the first).
 __device__ unsigned int g_stage_timeouts;
+
+__device__ __forceinline__ int lane_id() { return (int)(threadIdx.x & 31); }
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
     return (unsigned)__cvta_generic_to_shared(p);
@@ -107,7 +114,7 @@ __device__ __forceinline__ void bulk_load(unsigned dst, const void* src, unsigne
 // the nsc blocks from block blk0 on, behind the chunk (32-byte areas).  Every
 // lane must have finished its accesses of the slot and fenced them against
 // the async proxy before.
-template <typename GT>
+template <typename GT, int LAYOUT = MDQ_LAYOUT_S8U8>
 __device__ __forceinline__ void stage_chunk(const TensorPtrs& T, int64_t e0, unsigned dst,
                                             unsigned bar, unsigned long long policy,
                                             int64_t blk0 = 0, int nsc = 0) {
@@ -115,12 +122,13 @@ __device__ __forceinline__ void stage_chunk(const TensorPtrs& T, int64_t e0, uns
     constexpr unsigned kG = (unsigned)sizeof(GT) * C;
     const unsigned sb = 4u * (unsigned)nsc;
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                 "r"((unsigned)stg_chunk_bytes<GT>() + 3 * sb)
+                 "r"((unsigned)stg_copy_bytes<GT, LAYOUT>() + 3 * sb)
                  : "memory");
     bulk_load(dst, T.p + e0, 4 * C, bar, policy);
     bulk_load(dst + 4 * C, static_cast<const GT*>(T.g) + e0, kG, bar, policy);
     bulk_load(dst + 4 * C + kG, static_cast<const int8_t*>(T.m) + e0, C, bar, policy);
-    bulk_load(dst + 5 * C + kG, static_cast<const uint8_t*>(T.v) + e0, C, bar, policy);
+    if (LAYOUT != MDQ_LAYOUT_PACKED4)
+        bulk_load(dst + 5 * C + kG, static_cast<const uint8_t*>(T.v) + e0, C, bar, policy);
     if (nsc > 0) {
         const unsigned so = (unsigned)stg_chunk_bytes<GT>();
         bulk_load(dst + so, T.sm + blk0, sb, bar, policy);
@@ -298,15 +306,17 @@ __device__ __forceinline__ bool staged_block_body(const TileCtx& X, int64_t e0,
 // all NBU blocks, instead of one per lane and block), lanes < NBU store the
 // new scales, and pass 2 takes each block's constants from lane b by shuffle.
 // Returns false when a wait ran out.
-template <typename GT, bool EXACT_P, int LOGB>
+template <int LAYOUT, typename GT, bool EXACT_P, int LOGB>
 __device__ __forceinline__ bool staged_small_body(const TileCtx& X, int64_t e0,
                                                   const ParkRing<GT, 2>& park,
                                                   const unsigned (&bars)[2],
                                                   const unsigned (&par)[2]) {
-    using CI = Codes<MDQ_LAYOUT_S8U8>;
+    using CI = Codes<LAYOUT>;
     constexpr int C = kChunk;
     constexpr int kG = (int)sizeof(GT) * C;
     constexpr int NBU = stg_nbu<LOGB>();
+    constexpr bool kPacked = LAYOUT == MDQ_LAYOUT_PACKED4;
+    const float kf = small_int_to_float(lane_id() & 15);   // table entry of this lane
     const float kNaN = __int_as_float(0x7fffffff);
     const int lane = threadIdx.x & 31;
     const TensorPtrs T = X.t;
@@ -340,6 +350,25 @@ __device__ __forceinline__ bool staged_small_body(const TileCtx& X, int64_t e0,
             GradRaw<GT>::decode(gw, gg);
             g[2 * i] = make_float2(gg[0], gg[1]);
             g[2 * i + 1] = make_float2(gg[2], gg[3]);
+            if constexpr (kPacked) {
+                // 16-entry tables of the block's dequantised values
+                // (CUDA/stquant_kernel.cu:163-169), entry lane % 16, read
+                // with one 16-wide shuffle per value indexed by the nibble.
+                const float tv = dequant_v(kf, sv, vmn);
+                const float tm = __fmul_rn(__fsub_rn(kf, 8.0f), sm);
+                const unsigned cw = *reinterpret_cast<const unsigned*>(chunk + 4 * C + kG + k);
+                float mv[4], vv[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    mv[j] = __shfl_sync(0xffffffffu, tm, (int)(cw >> (8 * j)), 16);
+                    vv[j] = __shfl_sync(0xffffffffu, tv, (int)(cw >> (8 * j + 4)), 16);
+                }
+                m[2 * i] = make_float2(mv[0], mv[1]);
+                m[2 * i + 1] = make_float2(mv[2], mv[3]);
+                v[2 * i] = make_float2(vv[0], vv[1]);
+                v[2 * i + 1] = make_float2(vv[2], vv[3]);
+                continue;
+            }
             const unsigned mw = *reinterpret_cast<const unsigned*>(chunk + 4 * C + kG + k) ^ 0x80808080u;
             const unsigned vw = *reinterpret_cast<const unsigned*>(chunk + 5 * C + kG + k);
 #pragma unroll
@@ -474,7 +503,7 @@ __device__ __forceinline__ bool staged_small_body(const TileCtx& X, int64_t e0,
 // unit whose chunks were not issued ahead (the warp's first unit of a
 // tensor) issues them at once.  Other units (tails, unaligned tensors) run
 // the direct-load body of mdq_blocks.cuh, parking in the ring.
-template <typename GT, bool EXACT_P, int CAP, int LOGB>
+template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB>
 __global__ void __launch_bounds__(32 * stg_warps<GT, LOGB>(), stg_min_ctas<GT, LOGB>())
 mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
     constexpr int W = stg_warps<GT, LOGB>();
@@ -488,6 +517,7 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
     constexpr bool kSmall = LOGB < 9;
     static_assert(kSmall || NS * kCh >= 2 * B * (int)sizeof(float),
                   "the ring holds a direct-path park");
+    static_assert(kSmall || LAYOUT == MDQ_LAYOUT_S8U8, "packed 4-bit codes: small blocks only");
     extern __shared__ __align__(128) char s_ring[];
     __shared__ TileCtx s_wctx[W];
     __shared__ __align__(8) unsigned long long s_bar[W][NS];
@@ -569,7 +599,7 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
             par[c] = (parity >> pos[c]) & 1u;
             if (stage_cur && held_at(pos[c]) != u * CPB + c) {
                 if (lane == 0)
-                    stage_chunk<GT>(X.t, e0 + c * kChunk, ring_s + pos[c] * kCh, bars[c], policy,
+                    stage_chunk<GT, LAYOUT>(X.t, e0 + c * kChunk, ring_s + pos[c] * kCh, bars[c], policy,
                                     e0 >> LOGB, kSmall && c == 0 ? NBU : 0);
                 set_held(pos[c], u * CPB + c);
             }
@@ -577,14 +607,14 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
         const int fpos = base + CPB >= NS ? base + CPB - NS : base + CPB;   // the free slot
         if (stage_next) {
             if (lane == 0)
-                stage_chunk<GT>(X.t, e2, ring_s + fpos * kCh, bar0 + 8 * fpos, policy, e2 >> LOGB,
+                stage_chunk<GT, LAYOUT>(X.t, e2, ring_s + fpos * kCh, bar0 + 8 * fpos, policy, e2 >> LOGB,
                                 kSmall ? NBU : 0);
             set_held(fpos, u2 * CPB);
         }
         if (stage_cur) {
             bool ok;
             if constexpr (kSmall)
-                ok = staged_small_body<GT, EXACT_P, LOGB>(X, e0, park, bars, par);
+                ok = staged_small_body<LAYOUT, GT, EXACT_P, LOGB>(X, e0, park, bars, par);
             else
                 ok = staged_block_body<GT, EXACT_P, LOGB>(X, e0, park, bars, par);
             if (!ok) {
@@ -621,7 +651,7 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
 #pragma unroll
             for (int c = 1; c < CPB; ++c) {
                 if (lane == 0)
-                    stage_chunk<GT>(X.t, e2 + c * kChunk, ring_s + pos[c - 1] * kCh,
+                    stage_chunk<GT, LAYOUT>(X.t, e2 + c * kChunk, ring_s + pos[c - 1] * kCh,
                                     bar0 + 8 * pos[c - 1], policy);
                 set_held(pos[c - 1], u2 * CPB + c);
             }
@@ -630,9 +660,9 @@ mdq_step_staged(const __grid_constant__ LaunchParams<CAP> P) {
     }
 }
 
-template <typename GT, bool EXACT_P, int CAP, int LOGB>
+template <int LAYOUT, typename GT, bool EXACT_P, int CAP, int LOGB>
 mdq_status launch_staged_t(const LaunchParams<CAP>& P, int sms, cudaStream_t stream) {
-    auto k = mdq_step_staged<GT, EXACT_P, CAP, LOGB>;
+    auto k = mdq_step_staged<LAYOUT, GT, EXACT_P, CAP, LOGB>;
     constexpr int W = stg_warps<GT, LOGB>();
     constexpr int kSmem = stg_smem_bytes<GT, LOGB>();
     {
@@ -658,10 +688,13 @@ mdq_status launch_staged_t(const LaunchParams<CAP>& P, int sms, cudaStream_t str
     return MDQ_OK;
 }
 
-// int8/uint8 codes, blocks of 2^logb (9 or 10) elements, no peers and no
-// gradient ranks.
+// Blocks of 2^logb elements, no peers and no gradient ranks: int8/uint8
+// codes with logb 7..10, packed 4-bit codes with logb 7 or 8.
 template <int CAP>
 mdq_status launch_staged_s8u8(int gdt, const LaunchParams<CAP>& P, bool exact, int logb, int sms,
                               cudaStream_t s);
+template <int CAP>
+mdq_status launch_staged_packed4(int gdt, const LaunchParams<CAP>& P, bool exact, int logb, int sms,
+                                 cudaStream_t s);
 
 }  // namespace mdq

@@ -10,10 +10,10 @@ mdq_status launch_staged_s8u8(int gdt, const LaunchParams<CAP>& P, bool exact, i
 #define MDQ_STAGED_CASE(L)                                                                   \
     case L:                                                                                  \
         if (gdt == MDQ_BF16)                                                                 \
-            return exact ? launch_staged_t<__nv_bfloat16, true, CAP, L>(P, sms, s)            \
-                         : launch_staged_t<__nv_bfloat16, false, CAP, L>(P, sms, s);          \
-        return exact ? launch_staged_t<float, true, CAP, L>(P, sms, s)                        \
-                     : launch_staged_t<float, false, CAP, L>(P, sms, s);
+            return exact ? launch_staged_t<MDQ_LAYOUT_S8U8, __nv_bfloat16, true, CAP, L>(P, sms, s)            \
+                         : launch_staged_t<MDQ_LAYOUT_S8U8, __nv_bfloat16, false, CAP, L>(P, sms, s);          \
+        return exact ? launch_staged_t<MDQ_LAYOUT_S8U8, float, true, CAP, L>(P, sms, s)                        \
+                     : launch_staged_t<MDQ_LAYOUT_S8U8, float, false, CAP, L>(P, sms, s);
     switch (logb) {
         MDQ_STAGED_CASE(7)
         MDQ_STAGED_CASE(8)

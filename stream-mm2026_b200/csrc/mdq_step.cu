@@ -47,6 +47,10 @@ namespace mdq {
 template <int CAP>
 mdq_status launch_staged_s8u8(int gdt, const LaunchParams<CAP>& P, bool exact, int logb, int sms,
                               cudaStream_t s);
+// The same for packed 4-bit codes at 128/256-element blocks (mdq_staged_packed4.cu).
+template <int CAP>
+mdq_status launch_staged_packed4(int gdt, const LaunchParams<CAP>& P, bool exact, int logb, int sms,
+                                 cudaStream_t s);
 }  // namespace mdq
 
 // The C layout the Python mirror (mdq_b200/kernels.py, _lib.py) packs.
@@ -217,10 +221,12 @@ bool vec_ok(const mdq_tensor_desc& d) {
 }
 
 // Bit 1 of LaunchDesc::vec: every streamed array starts on a 16-byte
-// boundary, as bulk copies into shared memory need (int8/uint8 codes).
+// boundary, as bulk copies into shared memory need (int8/uint8 and packed
+// 4-bit codes).
 bool bulk_ok(const mdq_tensor_desc& d) {
-    return d.layout == MDQ_LAYOUT_S8U8 && aligned(d.p, 16) && aligned(d.grad, 16) &&
-           aligned(d.exp_avg, 16) && aligned(d.exp_avg_sq, 16);
+    if (!(aligned(d.p, 16) && aligned(d.grad, 16) && aligned(d.exp_avg, 16))) return false;
+    if (d.layout == MDQ_LAYOUT_S8U8) return aligned(d.exp_avg_sq, 16);
+    return d.layout == MDQ_LAYOUT_PACKED4;
 }
 
 bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
@@ -363,7 +369,16 @@ bool use_staged_kernel(int layout, int block, bool exact, const mdq::PeerSet& pe
         const char* e = getenv("MDQ_STAGED");
         mode = e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
     }
-    if (layout != MDQ_LAYOUT_S8U8 || peers.n != 0 || granks.n != 0) return false;
+    if (peers.n != 0 || granks.n != 0) return false;
+    if (layout == MDQ_LAYOUT_PACKED4) {
+        // Packed 4-bit codes, fast p (staged vs tiled, Gparams/s): 128-element
+        // blocks 404 vs 359, 256-element blocks 423 vs 422; the tiled kernel's
+        // tables serve the larger blocks.  MDQ_STAGED=1 also takes 256.
+        if (exact || block > 256) return false;
+        if (mode >= 0) return mode == 1;
+        return block == 128;
+    }
+    if (layout != MDQ_LAYOUT_S8U8) return false;
     if (mode >= 0) return mode == 1;
     return !(exact && (block == 1024 || block <= 256));
 }
@@ -428,13 +443,15 @@ bool bulk_ok_small(const mdq_tensor_desc& d) {
     return bulk_ok(d) && aligned(d.scale_m, 16) && aligned(d.scale_v, 16) && aligned(d.v_min, 16);
 }
 
-// The same int8/uint8 tensor from element `off` on (a multiple of its block).
+// The same tensor from element `off` on (a multiple of its block).
 mdq_tensor_desc desc_from(const mdq_tensor_desc& d, int64_t off) {
     mdq_tensor_desc r = d;
     const int64_t gsz = d.grad_dtype == MDQ_BF16 ? 2 : 4;
     r.p = d.p + off;
     r.grad = static_cast<const char*>(d.grad) + off * gsz;
-    r.exp_avg = static_cast<char*>(d.exp_avg) + off * storage_bits_m(d.layout) / 8;
+    // (packed 4-bit codes: one byte per element, both nibbles)
+    const int64_t mbytes = d.layout == MDQ_LAYOUT_PACKED4 ? 8 : storage_bits_m(d.layout);
+    r.exp_avg = static_cast<char*>(d.exp_avg) + off * mbytes / 8;
     if (d.exp_avg_sq != nullptr)
         r.exp_avg_sq = static_cast<char*>(d.exp_avg_sq) + off * storage_bits_v(d.layout) / 8;
     r.scale_m = d.scale_m + off / d.block;
@@ -498,8 +515,11 @@ mdq_status run_class(const mdq_tensor_desc* descs, const int* idx, int count, bo
                 ++i;
             }
             P.total_tiles = (int32_t)units;
-            const mdq_status st = mdq::launch_staged_s8u8<CAP>(descs[staged[0]].grad_dtype, P,
-                                                               exact, logb, sms, s);
+            const int gdt = descs[staged[0]].grad_dtype;
+            const mdq_status st =
+                layout == MDQ_LAYOUT_PACKED4
+                    ? mdq::launch_staged_packed4<CAP>(gdt, P, exact, logb, sms, s)
+                    : mdq::launch_staged_s8u8<CAP>(gdt, P, exact, logb, sms, s);
             if (st != MDQ_OK) return st;
         }
         if (rest.empty()) return MDQ_OK;

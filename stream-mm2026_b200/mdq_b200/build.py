@@ -25,7 +25,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libmdq.so")
 SOURCES = ["mdq_step.cu", "mdq_stats.cu", "mdq_tiles_packed4.cu", "mdq_tiles_s8u8.cu",
            "mdq_tiles_s16u16.cu", "mdq_tiles_s32u32.cu", "mdq_tiles_m8v4.cu",
            "mdq_blocks_packed4.cu", "mdq_blocks_s8u8.cu", "mdq_blocks_s16u16.cu",
-           "mdq_blocks_s32u32.cu", "mdq_blocks_m8v4.cu", "mdq_staged_s8u8.cu",
+           "mdq_blocks_s32u32.cu", "mdq_blocks_m8v4.cu", "mdq_staged_s8u8.cu", "mdq_staged_packed4.cu",
            "mdq_fakequant.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -120,33 +120,45 @@ def test_multi_tensor_matches_single(ref, cuda_device):
             assert all(v == 0 for v in mm.values()), f"step {s}: {mm}"
 
 
-@pytest.mark.parametrize("block", [128, 256, 512, 1024])
+STAGED_CASES = [("s8u8", 8, b) for b in (128, 256, 512, 1024)] + \
+    [("packed4", 4, b) for b in (128, 256)]
+
+
+@pytest.mark.parametrize("layout,bits,block", STAGED_CASES)
 @pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16])
-def test_int8_codes_many_tensors(ref, cuda_device, block, gdt):
-    """int8/uint8 codes at 128..1024-element blocks (the staged kernels; at 128
-    and 256 each tensor's last n mod 1024 elements go to the tiled kernel),
-    several tensors in one call:
-    tensors that start and end inside a CTA's share of blocks, tails, a tensor
-    of one block, one shorter than a block, and one whose m codes start 8
-    bytes past a 16-byte boundary (no bulk copies for it) == reference."""
+@pytest.mark.parametrize("p_mode", [P_EXACT, P_FAST])
+def test_staged_codes_many_tensors(ref, cuda_device, layout, bits, block, gdt, p_mode):
+    """The bulk-copy staged kernels (int8/uint8 codes at 128..1024-element
+    blocks, packed 4-bit codes at 128/256 in fast p mode; at 128 and 256 each
+    tensor's last n mod 1024 elements go to the tiled kernel), several tensors
+    in one call: tensors that start and end inside a CTA's share of units,
+    tails, a tensor of one block, one shorter than a block, and one whose m
+    codes start 8 bytes past a 16-byte boundary (no bulk copies for it) ==
+    reference.  Codes and scales bit for bit; parameters bit for bit in exact
+    mode, within 1e-6 of max|p| in fast mode."""
     sizes = [3 * block, 50 * block + 17, 100, 700 * block, block, 5000, 64 * block + 1]
-    refs = [State(n, block, "s8u8", cuda_device, seed=i) for i, n in enumerate(sizes)]
+    refs = [State(n, block, layout, cuda_device, seed=i) for i, n in enumerate(sizes)]
     mine = [r.clone() for r in refs]
     odd = mine[1]
     buf = torch.empty(odd.n + 8, dtype=odd.m.dtype, device=cuda_device)
     odd.m = buf[8:8 + odd.n]
     odd.m.copy_(refs[1].m)
-    for s in range(1, 5):
+    for s in range(1, 6):
         items = []
         for i, (n, ra, mi) in enumerate(zip(sizes, refs, mine)):
             g = grads(n, 1, cuda_device, gdt, seed=100 * s + i)[0]
-            run_ref(ref, ra, g, s, 8)
-            items.append(item_of(mi, g, s, 8, 8, LAYOUT_S8U8))
-        kernels.step_multi(items, p_mode=P_EXACT)
+            run_ref(ref, ra, g, s, bits)
+            items.append(item_of(mi, g, s, bits, bits, LAYOUT_ID[layout]))
+        kernels.step_multi(items, p_mode=p_mode)
         torch.cuda.synchronize()
         for i, (ra, mi) in enumerate(zip(refs, mine)):
             mm = ra.mismatches(mi)
-            assert all(v == 0 for v in mm.values()), f"step {s} tensor {i}: {mm}"
+            keys = ("p", "m", "v", "sm", "sv", "vmin") if p_mode == P_EXACT else \
+                ("m", "v", "sm", "sv", "vmin")
+            assert all(mm[k] == 0 for k in keys), f"step {s} tensor {i}: {mm}"
+            if p_mode == P_FAST:
+                err = (ra.p - mi.p).abs().max().item()
+                assert err <= 1e-6 * max(ra.p.abs().max().item(), 1e-30), (i, err)
 
 
 def test_many_tensors_one_launch(ref, cuda_device):
