@@ -657,9 +657,10 @@ def traffic_per_launch(n_elems):
     """DRAM bytes per launch from the committed ncu summary of this kernel,
     scaled from its capture size to this launch (traffic is proportional)."""
     lay = "packed4" if BITS == 4 else "s8u8"
-    # int8/uint8 codes at 512/1024-element blocks run the staged
-    # warp-per-block kernel.
-    kern = "mdq_step_staged" if BITS == 8 and BLOCK in (512, 1024) else "mdq_step_tiles"
+    # int8/uint8 codes at 128..1024-element blocks and packed 4-bit codes at
+    # 128-element blocks run the staged kernel (fast p).
+    staged = (BITS == 8 and BLOCK in (128, 256, 512, 1024)) or (BITS == 4 and BLOCK == 128)
+    kern = "mdq_step_staged" if staged else "mdq_step_tiles"
     path = os.path.join(REPO, "profiles", f"{kern}_{lay}_bf16_b{BLOCK}.json")
     full = os.path.join(REPO, "profiles", f"{kern}_{lay}_bf16_b{BLOCK}_2e{LOG2_N}.json")
     if os.path.exists(full):
